@@ -1,0 +1,55 @@
+// Python bindings of the revpp CUDA extension (module revpp._C).
+#include <torch/extension.h>
+
+#include "host.h"
+
+namespace revpp {
+// gemm.cu
+void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
+             int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
+             const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits);
+int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K);
+// norm.cu
+void layernorm_fwd(const torch::Tensor& x, const torch::Tensor& gamma, const torch::Tensor& beta, double eps,
+                   const c10::optional<torch::Tensor>& y_bf16, const c10::optional<torch::Tensor>& y_f32,
+                   const c10::optional<torch::Tensor>& y2_f32, const c10::optional<torch::Tensor>& mean,
+                   const c10::optional<torch::Tensor>& rstd);
+void layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& gamma,
+                   const torch::Tensor& mean, const torch::Tensor& rstd, const c10::optional<torch::Tensor>& dgamma,
+                   const c10::optional<torch::Tensor>& dbeta, const c10::optional<torch::Tensor>& resid,
+                   const c10::optional<torch::Tensor>& dx_f32, const c10::optional<torch::Tensor>& dx_bf16,
+                   const c10::optional<torch::Tensor>& colsum);
+void cast_colsum(const torch::Tensor& in, const c10::optional<torch::Tensor>& out,
+                 const c10::optional<torch::Tensor>& colsum);
+// attention.cu
+void attn_fwd(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S, int64_t heads);
+void attn_bwd(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout, const torch::Tensor& lse,
+              torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B, int64_t S, int64_t heads);
+}  // namespace revpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "revpp sm_100a kernels";
+  m.def("status_peek", &revpp::status_peek, "Read the device error word of the current device");
+  m.def("status_read_and_clear", &revpp::status_read_and_clear, "Read and clear the device error word");
+  m.def("num_sms", &revpp::num_sms);
+
+  m.def("gemm_tc", &revpp::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
+        py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("C"),
+        py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("aux_out") = py::none(),
+        py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1);
+  m.def("gemm_suggest_splits", &revpp::gemm_suggest_splits);
+
+  m.def("layernorm_fwd", &revpp::layernorm_fwd, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps"),
+        py::arg("y_bf16") = py::none(), py::arg("y_f32") = py::none(), py::arg("y2_f32") = py::none(),
+        py::arg("mean") = py::none(), py::arg("rstd") = py::none());
+  m.def("layernorm_bwd", &revpp::layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("gamma"), py::arg("mean"),
+        py::arg("rstd"), py::arg("dgamma") = py::none(), py::arg("dbeta") = py::none(), py::arg("resid") = py::none(),
+        py::arg("dx_f32") = py::none(), py::arg("dx_bf16") = py::none(), py::arg("colsum") = py::none());
+  m.def("attn_fwd", &revpp::attn_fwd, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"),
+        py::arg("heads"));
+  m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
+        py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
+  m.def("cast_colsum", &revpp::cast_colsum, py::arg("inp"), py::arg("out") = py::none(),
+        py::arg("colsum") = py::none());
+}

@@ -1,0 +1,495 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[M,N] (op)= A[M,K] * B[N,K]^T       bf16 operands, fp32 accumulation in TMEM
+//
+// Operands may be K-major (row-major [rows, K]) or MN-major (stored as [K, rows]);
+// this covers forward (A K, B K), input-gradient (A K, B MN: the weight [N_out, K_in]
+// read as [K_in rows] x [N_out reduction]) and weight-gradient (A MN, B MN: the
+// activations [tokens, features] read along the token reduction) GEMMs without any
+// transposed copies.
+//
+// Warp roles (320 threads):
+//   warp 0      : TMA producer (one thread), STAGES-deep smem ring, no multicast
+//   warp 1      : TMEM allocator + MMA issuer (one thread), tcgen05.mma 128xBNx16
+//   warps 2..9  : epilogue; TMEM -> registers (tcgen05.ld) -> fused op -> global
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of
+// tile i overlaps the main loop of tile i+1.
+//
+// Replaces the reference's cuBLAS GEMMs inside nn.Linear / nn.MultiheadAttention
+// (BERT/models/bert_blocks.py:34-63) and their autograd backward.
+#include "common.cuh"
+#include "host.h"
+
+namespace revpp {
+
+enum GemmEpi : int {
+  kEpiBF16 = 0,       // C_bf16 = bf16(acc + bias)
+  kEpiGelu = 1,       // u = bf16(acc + bias); C_bf16 = bf16(gelu(u)); aux_out = u
+  kEpiResid = 2,      // C_f32 = resid + sign * bf16(acc + bias)     (reversible coupling)
+  kEpiAtomicF32 = 3,  // C_f32 += acc  (vector atomics; split-K and grad accumulation)
+  kEpiDGelu = 4,      // C_bf16 = bf16(bf16(acc) * gelu'(aux))         (GELU backward)
+  kEpiF32 = 5,        // C_f32 = acc + bias
+  kEpiCount = 6,
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_per_split, kb_total;
+  void* C;
+  long long ldc;
+  const __nv_bfloat16* bias;  // [N] or null
+  const __nv_bfloat16* aux;   // [M, ld_aux] bf16 (pre-activation for kEpiDGelu)
+  __nv_bfloat16* aux_out;     // [M, ld_aux] bf16 (pre-activation written by kEpiGelu) or null
+  long long ld_aux;
+  const float* resid;  // [M, ld_resid] fp32 (kEpiResid)
+  long long ld_resid;
+  float sign;
+  int* status;
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmEpiWarps = 8;
+constexpr int kGemmThreads = 64 + kGemmEpiWarps * 32;
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&r)[32]) {
+  if (row >= a.M || col0 >= a.N) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+
+  if constexpr (EPI == kEpiAtomicF32) {
+    float* c = reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      atomicAdd(reinterpret_cast<float4*>(c + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+    }
+    return;
+  } else {
+    if (a.bias != nullptr && EPI != kEpiDGelu) {
+      const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 b = __ldg(bp + j);
+        const float2 b0 = unpack_bf16x2(b.x), b1 = unpack_bf16x2(b.y), b2 = unpack_bf16x2(b.z),
+                     b3 = unpack_bf16x2(b.w);
+        v[8 * j + 0] += b0.x; v[8 * j + 1] += b0.y; v[8 * j + 2] += b1.x; v[8 * j + 3] += b1.y;
+        v[8 * j + 4] += b2.x; v[8 * j + 5] += b2.y; v[8 * j + 6] += b3.x; v[8 * j + 7] += b3.y;
+      }
+    }
+    if constexpr (EPI == kEpiBF16) {
+      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        c[j] = make_uint4(pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                          pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+      }
+    } else if constexpr (EPI == kEpiGelu) {
+      float h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = bf16r(v[j]);
+        h[j] = gelu_erf(v[j]);
+      }
+      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        c[j] = make_uint4(pack_bf16x2(h[8 * j + 0], h[8 * j + 1]), pack_bf16x2(h[8 * j + 2], h[8 * j + 3]),
+                          pack_bf16x2(h[8 * j + 4], h[8 * j + 5]), pack_bf16x2(h[8 * j + 6], h[8 * j + 7]));
+      }
+      if (a.aux_out != nullptr) {
+        uint4* u = reinterpret_cast<uint4*>(a.aux_out + static_cast<long long>(row) * a.ld_aux + col0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          u[j] = make_uint4(pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+        }
+      }
+    } else if constexpr (EPI == kEpiResid) {
+      const float4* rs = reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row) * a.ld_resid + col0);
+      float4* c = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+      const float s = a.sign;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = rs[j];
+        c[j] = make_float4(x.x + s * bf16r(v[4 * j + 0]), x.y + s * bf16r(v[4 * j + 1]), x.z + s * bf16r(v[4 * j + 2]),
+                           x.w + s * bf16r(v[4 * j + 3]));
+      }
+    } else if constexpr (EPI == kEpiDGelu) {
+      const uint4* up = reinterpret_cast<const uint4*>(a.aux + static_cast<long long>(row) * a.ld_aux + col0);
+      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = up[j];
+        const float2 u0 = unpack_bf16x2(u.x), u1 = unpack_bf16x2(u.y), u2 = unpack_bf16x2(u.z), u3 = unpack_bf16x2(u.w);
+        const float g0 = bf16r(v[8 * j + 0]) * gelu_erf_grad(u0.x), g1 = bf16r(v[8 * j + 1]) * gelu_erf_grad(u0.y);
+        const float g2 = bf16r(v[8 * j + 2]) * gelu_erf_grad(u1.x), g3 = bf16r(v[8 * j + 3]) * gelu_erf_grad(u1.y);
+        const float g4 = bf16r(v[8 * j + 4]) * gelu_erf_grad(u2.x), g5 = bf16r(v[8 * j + 5]) * gelu_erf_grad(u2.y);
+        const float g6 = bf16r(v[8 * j + 6]) * gelu_erf_grad(u3.x), g7 = bf16r(v[8 * j + 7]) * gelu_erf_grad(u3.y);
+        c[j] = make_uint4(pack_bf16x2(g0, g1), pack_bf16x2(g2, g3), pack_bf16x2(g4, g5), pack_bf16x2(g6, g7));
+      }
+    } else if constexpr (EPI == kEpiF32) {
+      float4* c = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  constexpr int BM = kGemmBM, BK = kGemmBK;
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
+  static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM alloc must be a power of 2");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull[0], 1);
+    mbar_init(&tfull[1], 1);
+    mbar_init(&tempty[0], kGemmEpiWarps);
+    mbar_init(&tempty[1], kGemmEpiWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;  // per-stage bits, for the drain on abort
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int tm = t % args.tiles_m;
+        const int rest = t / args.tiles_m;
+        const int tn = rest % args.tiles_n;
+        const int ts = rest / args.tiles_n;
+        const int kb0 = ts * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, abort_flag)) goto producer_abort;
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, tm * BM);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_2d(a_dst + c * (BK * 128), &tmA, &full[stage], tm * BM + c * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, tn * BN);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(b_dst + c * (BK * 128), &tmB, &full[stage], tn * BN + c * 64, kb * BK);
+          }
+          issued |= (1u << stage);
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      goto producer_end;
+    producer_abort:
+      // Let every copy this thread issued land before the CTA leaves.
+      for (int s = 0; s < STAGES; ++s) {
+        if (issued & (1u << s)) {
+          const uint32_t par = (issued_parity >> s) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], par) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    producer_end:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      const uint32_t a_base = smem_u32(sA);
+      const uint32_t b_base = smem_u32(sB);
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int rest = t / args.tiles_m;
+        const int ts = rest / args.tiles_n;
+        const int kb0 = ts * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_s = a_base + stage * A_BYTES;
+          const uint32_t b_s = b_base + stage * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_s + k * 2048, BK * 128, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_s + k * 2048, BK * 128, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // All MMAs of this thread complete before TMEM is released.
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;     // TMEM lane quarter this warp may access
+    const int half = ew >> 2;   // column half handled by this warp
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int tm = t % args.tiles_m;
+      const int tn = (t / args.tiles_m) % args.tiles_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
+      tc_fence_after();
+      const int row = tm * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 64; ++c) {
+        const int ccol = half * (BN / 2) + c * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + ccol), r);
+        tmem_wait_ld();
+        gemm_epilogue_chunk<EPI>(args, row, tn * BN + ccol, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                      cudaStream_t st) {
+  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024 + 256;
+  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static int configured_for = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_for != dev) {
+    REVPP_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured_for = dev;
+  }
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, args);
+  REVPP_CHECK_LAUNCH();
+}
+
+// Only the operand-layout / epilogue pairs the models use are instantiated:
+//   A K-major, B K-major : forward GEMMs       (bf16, gelu, residual, f32)
+//   A K-major, B MN-major: input-gradient GEMMs (bf16, gelu-backward, f32)
+//   A MN-major, B MN-major: weight gradients   (atomic f32 accumulate)
+void dispatch_gemm(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                   const GemmArgs& args, int grid, cudaStream_t st) {
+  constexpr int BN = 256, ST = 4;
+  if (!a_mn && !b_mn) {
+    switch (epi) {
+      case kEpiBF16: return launch_gemm_inst<BN, ST, false, false, kEpiBF16>(ta, tb, args, grid, st);
+      case kEpiGelu: return launch_gemm_inst<BN, ST, false, false, kEpiGelu>(ta, tb, args, grid, st);
+      case kEpiResid: return launch_gemm_inst<BN, ST, false, false, kEpiResid>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm_inst<BN, ST, false, false, kEpiF32>(ta, tb, args, grid, st);
+      default: break;
+    }
+  } else if (!a_mn && b_mn) {
+    switch (epi) {
+      case kEpiBF16: return launch_gemm_inst<BN, ST, false, true, kEpiBF16>(ta, tb, args, grid, st);
+      case kEpiDGelu: return launch_gemm_inst<BN, ST, false, true, kEpiDGelu>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm_inst<BN, ST, false, true, kEpiF32>(ta, tb, args, grid, st);
+      default: break;
+    }
+  } else if (a_mn && b_mn) {
+    if (epi == kEpiAtomicF32) return launch_gemm_inst<BN, ST, true, true, kEpiAtomicF32>(ta, tb, args, grid, st);
+  }
+  REVPP_CHECK(false, "GEMM layout/epilogue combination not built: a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+}  // namespace
+
+// A: if !a_mn, [M, K] row-major (row stride lda); if a_mn, [K, M] row-major.
+// B: if !b_mn, [N, K] row-major; if b_mn, [K, N] row-major.
+void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
+             int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
+             const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  REVPP_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm operands must be 2-D");
+  REVPP_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm operands need unit inner stride");
+  REVPP_CHECK(N % 32 == 0, "gemm N must be a multiple of 32, got ", N);
+  REVPP_CHECK(M > 0 && N > 0 && K > 0, "gemm sizes must be positive");
+  if (!a_mn) {
+    REVPP_CHECK(A.size(0) >= M && A.size(1) >= K, "A shape mismatch");
+  } else {
+    REVPP_CHECK(A.size(0) >= K && A.size(1) >= M, "A (MN-major) shape mismatch");
+  }
+  if (!b_mn) {
+    REVPP_CHECK(B.size(0) >= N && B.size(1) >= K, "B shape mismatch");
+  } else {
+    REVPP_CHECK(B.size(0) >= K && B.size(1) >= N, "B (MN-major) shape mismatch");
+  }
+  REVPP_CHECK(C.size(0) >= M && C.size(1) >= N, "C shape mismatch");
+  const bool c_f32 = (epi == kEpiResid || epi == kEpiAtomicF32 || epi == kEpiF32);
+  if (c_f32) {
+    check_cuda_f32(C, "C");
+  } else {
+    check_cuda_bf16(C, "C");
+  }
+  REVPP_CHECK((C.stride(0) * (c_f32 ? 4 : 2)) % 16 == 0, "C row stride must be a multiple of 16 bytes");
+  REVPP_CHECK(splits >= 1, "splits must be >= 1");
+  REVPP_CHECK(splits == 1 || epi == kEpiAtomicF32, "split-K needs the atomic epilogue");
+  c10::cuda::CUDAGuard guard(A.device());
+
+  GemmArgs args{};
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  args.tiles_m = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  args.tiles_n = static_cast<int>((N + 255) / 256);
+  args.kb_total = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  const int want_splits = static_cast<int>(std::min<int64_t>(splits, args.kb_total));
+  args.kb_per_split = (args.kb_total + want_splits - 1) / want_splits;
+  args.splits = (args.kb_total + args.kb_per_split - 1) / args.kb_per_split;
+  args.C = C.data_ptr();
+  args.ldc = C.stride(0);
+  args.bias = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    check_cuda_bf16(*bias, "bias");
+    REVPP_CHECK(bias->numel() >= N && bias->is_contiguous(), "bias must be contiguous [N]");
+    REVPP_CHECK((reinterpret_cast<uintptr_t>(bias->data_ptr()) & 15) == 0, "bias must be 16-byte aligned");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  args.aux = nullptr;
+  args.aux_out = nullptr;
+  args.ld_aux = 0;
+  if (epi == kEpiDGelu) {
+    REVPP_CHECK(aux.has_value() && aux->defined(), "DGelu epilogue needs aux (pre-activation)");
+    check_cuda_bf16(*aux, "aux");
+    REVPP_CHECK(aux->stride(1) == 1 && aux->size(0) >= M && aux->size(1) >= N);
+    args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    args.ld_aux = aux->stride(0);
+  }
+  if (epi == kEpiGelu && aux_out.has_value() && aux_out->defined()) {
+    check_cuda_bf16(*aux_out, "aux_out");
+    REVPP_CHECK(aux_out->stride(1) == 1 && aux_out->size(0) >= M && aux_out->size(1) >= N);
+    args.aux_out = reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr());
+    args.ld_aux = aux_out->stride(0);
+  }
+  args.resid = nullptr;
+  args.ld_resid = 0;
+  if (epi == kEpiResid) {
+    REVPP_CHECK(resid.has_value() && resid->defined(), "Resid epilogue needs resid");
+    check_cuda_f32(*resid, "resid");
+    REVPP_CHECK(resid->stride(1) == 1 && resid->size(0) >= M && resid->size(1) >= N);
+    args.resid = resid->data_ptr<float>();
+    args.ld_resid = resid->stride(0);
+  }
+  args.sign = static_cast<float>(sign);
+  args.status = status_device_ptr();
+
+  const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap ta, tb;
+  if (!a_mn) ta = make_tmap_2d(A.data_ptr(), bf, 2, K, M, A.stride(0) * 2, 64, kGemmBM, sw);
+  else ta = make_tmap_2d(A.data_ptr(), bf, 2, M, K, A.stride(0) * 2, 64, kGemmBK, sw);
+  if (!b_mn) tb = make_tmap_2d(B.data_ptr(), bf, 2, K, N, B.stride(0) * 2, 64, 256, sw);
+  else tb = make_tmap_2d(B.data_ptr(), bf, 2, N, K, B.stride(0) * 2, 64, kGemmBK, sw);
+
+  const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
+  const int grid = std::min(num_tiles, num_sms());
+  cudaStream_t st = cur_stream();
+  dispatch_gemm(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, grid, st);
+}
+
+// Split count that fills the machine for the weight-gradient GEMM.
+int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + 255) / 256);
+  const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
+  const int64_t sms = num_sms();
+  int64_t s = std::max<int64_t>(1, sms / std::max<int64_t>(tiles, 1));
+  s = std::min<int64_t>(s, std::max<int64_t>(1, kb / 4));  // keep >= 4 k-blocks per split
+  return s;
+}
+
+}  // namespace revpp

@@ -1,0 +1,62 @@
+// Host-side helpers shared by the revpp CUDA extension.
+#pragma once
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+// Argument checks throw std::runtime_error (pybind11 maps it to RuntimeError).
+// c10::Error thrown through host code built by g++ here crashed the process
+// instead of reaching Python, so the extension never uses TORCH_CHECK.
+#define REVPP_CHECK(cond, ...)                                                              \
+  do {                                                                                      \
+    if (!(cond)) {                                                                          \
+      throw std::runtime_error(c10::str("revpp: check failed [", #cond, "] at ", __FILE__, ":", \
+                                        __LINE__, " ", ##__VA_ARGS__));                     \
+    }                                                                                       \
+  } while (0)
+
+#define REVPP_CUDA_CHECK(expr)                                                                      \
+  do {                                                                                              \
+    cudaError_t _e = (expr);                                                                        \
+    REVPP_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " (", #expr, ")");         \
+  } while (0)
+
+#define REVPP_CHECK_LAUNCH() REVPP_CUDA_CHECK(cudaGetLastError())
+
+namespace revpp {
+
+// Device pointer of this process's status word for the current device.  Kernels
+// OR error bits into it; the host reads it through the mapped pinned page
+// without a device synchronisation.
+int* status_device_ptr();
+int status_peek();
+int status_read_and_clear();
+
+int num_sms();
+int max_smem_optin();
+
+// 2-D bf16 tensor map for TMA.  inner = elements of the contiguous dimension,
+// outer = number of rows, row_stride_bytes must be a multiple of 16.
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
+
+inline void check_cuda_bf16(const torch::Tensor& t, const char* name) {
+  REVPP_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  REVPP_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+inline void check_cuda_f32(const torch::Tensor& t, const char* name) {
+  REVPP_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  REVPP_CHECK(t.scalar_type() == at::kFloat, name, " must be float32");
+}
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+}  // namespace revpp

@@ -1,0 +1,51 @@
+"""Flash attention kernels against float64 PyTorch attention of the same bf16 inputs."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from revpp.ops._ext import ext
+
+    return ext()
+
+
+def _ref(qkv, B, S, heads):
+    H = heads * 64
+    x = qkv.double().view(B, S, 3, heads, 64)
+    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), x[:, :, 2].transpose(1, 2)
+    s = q @ k.transpose(-1, -2) / math.sqrt(64)
+    lse = torch.logsumexp(s, -1)
+    p = torch.softmax(s, -1)
+    o = (p @ v).transpose(1, 2).reshape(B * S, H)
+    return o, lse
+
+
+@pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3)])
+def test_attn_fwd_bwd(B, S, heads):
+    C = _C()
+    H = heads * 64
+    qkv = (torch.randn(B * S, 3 * H, device="cuda") * 1.5).to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    C.attn_fwd(qkv, out, lse, B, S, heads)
+    torch.cuda.synchronize()
+    qd = qkv.double().requires_grad_()
+    o_ref, lse_ref = _ref(qd, B, S, heads)
+    assert (out.double() - o_ref).abs().max().item() < 2e-2
+    assert (lse.double() - lse_ref).abs().max().item() < 2e-3
+
+    dout = torch.randn(B * S, H, device="cuda").to(torch.bfloat16)
+    dqkv = torch.empty_like(qkv)
+    dq_acc = torch.empty(B * S, H, device="cuda")
+    D = torch.empty(B, heads, S, device="cuda")
+    C.attn_bwd(qkv, out, dout, lse, dqkv, dq_acc, D, B, S, heads)
+    torch.cuda.synchronize()
+    o_ref.backward(dout.double())
+    g = qd.grad
+    err = (dqkv.double() - g).abs().max().item()
+    assert err < 3e-2 * (1 + g.abs().max().item()), err
+    assert C.status_read_and_clear() == 0

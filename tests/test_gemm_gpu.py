@@ -1,0 +1,132 @@
+"""tcgen05 GEMM numerics against a float64 PyTorch reference of the same op."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+EPI_BF16, EPI_GELU, EPI_RESID, EPI_ATOMIC, EPI_DGELU, EPI_F32 = range(6)
+
+SHAPES = [(128, 256, 64), (256, 512, 256), (300, 96, 200), (1000, 1024, 1024), (4096, 3072, 1024)]
+
+
+def _C():
+    from revpp.ops._ext import ext
+
+    return ext()
+
+
+def _rand(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+def _gelu(x):
+    return 0.5 * x * (1.0 + torch.erf(x / math.sqrt(2.0)))
+
+
+def _close(out, ref, rtol):
+    err = (out.double() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= rtol * scale, f"max abs err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_fwd_bias_bf16(M, N, K):
+    C = _C()
+    a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_BF16, out, bias=bias)
+    torch.cuda.synchronize()
+    assert C.status_read_and_clear() == 0
+    ref = a.double() @ b.double().t() + bias.double()
+    _close(out, ref, 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_fwd_gelu(M, N, K):
+    C = _C()
+    a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_GELU, out, bias=bias, aux_out=pre)
+    torch.cuda.synchronize()
+    u = a.double() @ b.double().t() + bias.double()
+    _close(pre, u, 1e-2)
+    _close(out, _gelu(pre.double()), 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("sign", [1.0, -1.0])
+def test_fwd_resid(M, N, K, sign):
+    C = _C()
+    a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
+    resid = torch.randn(M, N, device="cuda")
+    out = torch.empty(M, N, device="cuda")
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_RESID, out, bias=bias, resid=resid, sign=sign)
+    torch.cuda.synchronize()
+    f = (a.float() @ b.float().t() + bias.float()).to(torch.bfloat16).double()
+    ref = resid.double() + sign * f
+    # bf16 rounding of f may differ by one ulp from the float reference
+    _close(out, ref, 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_dgrad_mn(M, N, K):
+    """C[M,N] = A[M,K] @ W where W is stored [K, N] (MN-major B)."""
+    C = _C()
+    a, w = _rand(M, K), _rand(K, N, scale=0.05)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_BF16, out)
+    torch.cuda.synchronize()
+    _close(out, a.double() @ w.double(), 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_dgelu(M, N, K):
+    C = _C()
+    a, w = _rand(M, K), _rand(K, N, scale=0.05)
+    u = _rand(M, N)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u)
+    torch.cuda.synchronize()
+    ud = u.double()
+    dg = 0.5 * (1 + torch.erf(ud / math.sqrt(2))) + ud * torch.exp(-0.5 * ud * ud) / math.sqrt(2 * math.pi)
+    dh = (a.double() @ w.double()).to(torch.bfloat16).double()
+    _close(out, dh * dg, 2e-2)
+
+
+WGRAD_SHAPES = [(128, 256, 64), (256, 512, 256), (96, 160, 197 * 3), (1024, 1024, 1000), (3072, 1024, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", WGRAD_SHAPES)
+@pytest.mark.parametrize("splits", [1, 3])
+def test_wgrad_atomic(M, N, K, splits):
+    """C[M,N] += A^T B where A stored [K, M] and B stored [K, N] (both MN-major)."""
+    C = _C()
+    a, b = _rand(K, M), _rand(K, N)
+    out = torch.randn(M, N, device="cuda")
+    ref = out.double() + a.double().t() @ b.double()
+    C.gemm_tc(a, True, b, True, M, N, K, EPI_ATOMIC, out, splits=splits)
+    torch.cuda.synchronize()
+    _close(out, ref, 1e-4)
+
+
+def test_fwd_f32_persistent_many_tiles():
+    C = _C()
+    M, N, K = 8192, 4096, 512
+    a, b = _rand(M, K), _rand(N, K, scale=0.05)
+    out = torch.empty(M, N, device="cuda")
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_F32, out)
+    torch.cuda.synchronize()
+    _close(out, a.float() @ b.float().t(), 1e-4)
+    assert C.status_read_and_clear() == 0
+
+
+def test_bad_stride_raises():
+    """A row stride that TMA cannot describe is rejected with an exception, not a crash."""
+    C = _C()
+    a, b = _rand(200, 300), _rand(200, 96)
+    out = torch.zeros(300, 96, device="cuda")
+    with pytest.raises(RuntimeError):
+        C.gemm_tc(a, True, b, True, 300, 96, 200, EPI_ATOMIC, out)
