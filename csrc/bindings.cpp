@@ -26,6 +26,16 @@ void cast_colsum(const torch::Tensor& in, const c10::optional<torch::Tensor>& ou
 void attn_fwd(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S, int64_t heads);
 void attn_bwd(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout, const torch::Tensor& lse,
               torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B, int64_t S, int64_t heads);
+// optim.cu
+void grad_sumsq(const torch::Tensor& g, torch::Tensor out);
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v,
+                const c10::optional<torch::Tensor>& shadow, double lr, double beta1, double beta2, double eps,
+                double wd, int64_t step, double max_norm, const c10::optional<torch::Tensor>& sumsq,
+                bool zero_grad);
+void scale_(torch::Tensor x, double s);
+// host.cpp
+void set_sm_reserve(int n);
+int sm_reserve();
 }  // namespace revpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -33,6 +43,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_peek", &revpp::status_peek, "Read the device error word of the current device");
   m.def("status_read_and_clear", &revpp::status_read_and_clear, "Read and clear the device error word");
   m.def("num_sms", &revpp::num_sms);
+  m.def("set_sm_reserve", &revpp::set_sm_reserve, "SMs left free of persistent GEMM CTAs");
+  m.def("sm_reserve", &revpp::sm_reserve);
+  m.def("grad_sumsq", &revpp::grad_sumsq, py::arg("g"), py::arg("out"));
+  m.def("adamw_step", &revpp::adamw_step, py::arg("p"), py::arg("g"), py::arg("m"), py::arg("v"),
+        py::arg("shadow") = py::none(), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"),
+        py::arg("wd"), py::arg("step"), py::arg("max_norm"), py::arg("sumsq") = py::none(),
+        py::arg("zero_grad") = true);
+  m.def("scale_", &revpp::scale_, py::arg("x"), py::arg("s"));
 
   m.def("gemm_tc", &revpp::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("C"),

@@ -477,7 +477,7 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
   else tb = make_tmap_2d(B.data_ptr(), bf, 2, N, K, B.stride(0) * 2, 64, kGemmBK, sw);
 
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
-  const int grid = std::min(num_tiles, num_sms());
+  const int grid = std::min(num_tiles, gemm_grid_sms());
   cudaStream_t st = cur_stream();
   dispatch_gemm(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, grid, st);
 }

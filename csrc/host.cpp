@@ -64,6 +64,17 @@ int status_read_and_clear() {
   return v;
 }
 
+namespace {
+int g_sm_reserve = 0;
+}
+void set_sm_reserve(int n) { g_sm_reserve = n < 0 ? 0 : n; }
+int sm_reserve() { return g_sm_reserve; }
+
+int gemm_grid_sms() {
+  const int n = num_sms() - g_sm_reserve;
+  return n < 1 ? 1 : n;
+}
+
 int num_sms() {
   static int cached[kMaxDevices] = {0};
   const int d = current_device();

@@ -40,6 +40,11 @@ int status_peek();
 int status_read_and_clear();
 
 int num_sms();
+// SMs a persistent kernel may fill: all SMs minus those left free for concurrent
+// communication kernels (set_sm_reserve).
+int gemm_grid_sms();
+void set_sm_reserve(int n);
+int sm_reserve();
 int max_smem_optin();
 
 // 2-D bf16 tensor map for TMA.  inner = elements of the contiguous dimension,

@@ -1,0 +1,170 @@
+"""Stage-to-stage message channels.
+
+A ``Channel`` carries one kind of message (forward activations s -> s+1, or backward
+gradients + reconstructed inputs s+1 -> s) in one direction, over its own two-rank
+process group.  Because every channel has its own communicator (and so its own NCCL
+stream) and messages inside a channel are matched strictly in order, the forward and
+backward traffic of a stage pair can never block each other; the 1F1B send/recv pairing
+of the reference (BERT/pipelining/schedules.py:725-849, one fused batch_isend_irecv per
+step, waited synchronously) becomes free-running FIFO queues.
+
+Receives are posted ahead of use into a ring of ``depth`` preallocated slots; waiting on
+a receive makes the *current stream* wait for the NCCL stream (no host block on NCCL).
+Each slot carries a generation counter: reusing a slot whose previous message was never
+consumed raises (host-side race check).
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class TensorSpec:
+    shape: Tuple[int, ...]
+    dtype: torch.dtype
+
+
+@dataclass
+class _Pending:
+    slot: int
+    gen: int
+    works: list
+    tensors: List[torch.Tensor]
+
+
+class RingSlotError(RuntimeError):
+    pass
+
+
+class Channel:
+    def __init__(self, name: str, src: int, dst: int, group, specs: Sequence[TensorSpec], device: torch.device,
+                 depth: int = 2):
+        self.name = name
+        self.src = src
+        self.dst = dst
+        self.group = group
+        self.specs = list(specs)
+        self.device = device
+        self.depth = depth
+        self.rank = dist.get_rank()
+        self._slots: Optional[List[List[torch.Tensor]]] = None
+        self._slot_gen: List[int] = [0] * depth
+        self._slot_busy: List[bool] = [False] * depth
+        self._next_slot = 0
+        self._posted: Deque[_Pending] = deque()
+        self._send_inflight: Deque[Tuple[list, List[torch.Tensor]]] = deque()
+        self.sent = 0
+        self.received = 0
+
+    # -------------------------------------------------------------- receive side
+    def _alloc(self):
+        if self._slots is None:
+            self._slots = [[torch.empty(s.shape, dtype=s.dtype, device=self.device) for s in self.specs]
+                           for _ in range(self.depth)]
+
+    def post_recv(self) -> None:
+        """Post the receive of the next message into the next free ring slot."""
+        assert self.rank == self.dst, f"{self.name}: only rank {self.dst} receives"
+        self._alloc()
+        slot = self._next_slot
+        if self._slot_busy[slot]:
+            raise RingSlotError(f"{self.name}: ring slot {slot} (gen {self._slot_gen[slot]}) reused before its "
+                                f"message was consumed")
+        self._slot_busy[slot] = True
+        self._slot_gen[slot] += 1
+        bufs = self._slots[slot]
+        ops = [dist.P2POp(dist.irecv, t, self.src, self.group) for t in bufs]
+        works = dist.batch_isend_irecv(ops)
+        self._posted.append(_Pending(slot, self._slot_gen[slot], works, bufs))
+        self._next_slot = (slot + 1) % self.depth
+
+    @property
+    def posted(self) -> int:
+        return len(self._posted)
+
+    def recv(self) -> Tuple[List[torch.Tensor], int]:
+        """Oldest posted message.  The current stream waits for it; returns (tensors, slot)."""
+        if not self._posted:
+            self.post_recv()
+        p = self._posted.popleft()
+        for w in p.works:
+            w.wait()
+        self.received += 1
+        return p.tensors, p.slot
+
+    def release(self, slot: int) -> None:
+        """The consumer is done with a slot (its reads are enqueued on the current stream)."""
+        self._slot_busy[slot] = False
+
+    # -------------------------------------------------------------- send side
+    def send(self, tensors: Sequence[torch.Tensor]) -> None:
+        assert self.rank == self.src, f"{self.name}: only rank {self.src} sends"
+        ts = [t.contiguous() for t in tensors]
+        for t, s in zip(ts, self.specs):
+            if tuple(t.shape) != tuple(s.shape) or t.dtype != s.dtype:
+                raise ValueError(f"{self.name}: message {tuple(t.shape)}/{t.dtype} does not match "
+                                 f"{tuple(s.shape)}/{s.dtype}")
+        ops = [dist.P2POp(dist.isend, t, self.dst, self.group) for t in ts]
+        works = dist.batch_isend_irecv(ops)
+        self._send_inflight.append((works, ts))
+        self.sent += 1
+        self._reap()
+
+    def _reap(self, keep: int = 4) -> None:
+        # keep the last few sends' tensors alive; older ones are complete once waited
+        while len(self._send_inflight) > keep:
+            works, _ = self._send_inflight.popleft()
+            for w in works:
+                w.wait()
+
+    def drain(self) -> None:
+        while self._send_inflight:
+            works, _ = self._send_inflight.popleft()
+            for w in works:
+                w.wait()
+
+
+class PipeComms:
+    """All channels of one rank: forward/backward to both neighbours plus the label channel.
+
+    Process groups are created collectively by every rank in the same order (a requirement
+    of ``new_group``), for every pipeline replica."""
+
+    def __init__(self, rank: int, world: int, num_stages: int, replicas: int, device: torch.device,
+                 fwd_specs, bwd_specs, label_spec: Optional[TensorSpec], depth: int = 2):
+        self.rank = rank
+        self.P = num_stages
+        self.replica = rank // num_stages
+        self.stage = rank % num_stages
+        base = self.replica * num_stages
+        self.fwd_in = self.fwd_out = self.bwd_in = self.bwd_out = self.labels = None
+        backend = dist.get_backend()
+        for d in range(replicas):
+            b = d * num_stages
+            for s in range(num_stages - 1):
+                a, c = b + s, b + s + 1
+                g_f = dist.new_group([a, c], backend=backend)
+                g_b = dist.new_group([a, c], backend=backend)
+                if d == self.replica:
+                    if self.stage == s:
+                        self.fwd_out = Channel(f"fwd{s}->{s+1}", a, c, g_f, fwd_specs, device, depth)
+                        self.bwd_in = Channel(f"bwd{s+1}->{s}", c, a, g_b, bwd_specs, device, depth)
+                    if self.stage == s + 1:
+                        self.fwd_in = Channel(f"fwd{s}->{s+1}", a, c, g_f, fwd_specs, device, depth)
+                        self.bwd_out = Channel(f"bwd{s+1}->{s}", c, a, g_b, bwd_specs, device, depth)
+            if num_stages > 1 and label_spec is not None:
+                g_l = dist.new_group([b, b + num_stages - 1], backend=backend)
+                if d == self.replica and self.stage in (0, num_stages - 1):
+                    self.labels = Channel("labels", b, b + num_stages - 1, g_l, [label_spec], device, depth)
+        self.first_rank = base
+        self.last_rank = base + num_stages - 1
+
+    def drain(self) -> None:
+        for ch in (self.fwd_out, self.bwd_out, self.labels):
+            if ch is not None and ch.rank == ch.src:
+                ch.drain()

@@ -1,0 +1,153 @@
+"""Pipeline runtime on CPU / gloo against a plain-autograd oracle.
+
+Tiny reversible BERT, 2 pipeline stages x 2 reversible layers, fp32, global batch 16 in 4
+micro-batches of 4, token ids uniform in [0, 30522), all-ones mask, Bernoulli labels: the
+gradients of every parameter and the loss must match ordinary autograd through the same
+network (which stores every activation) to 1e-5.  The same harness checks the standard,
+activation-checkpoint, inverse and PaReprop variants and the 1F1B / GPipe schedules.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as Fn
+
+from revpp.config import build_global_config, parse_args
+from revpp.data import SyntheticBatches
+from revpp.engine import Trainer, runtime_kind
+from revpp.models.blockmath import TorchMath
+from revpp.models.encoder import TorchEmbedHead, build_stage_module, stage_kind
+from revpp.models.params import FlatParams
+from revpp.utils.env import build_env
+from revpp.utils.seed import set_seed
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _cfg(extra: str, world: int):
+    args = parse_args(("--preset tiny-bert --num-hidden-layers 4 --par-mode pp --batch-size 16 "
+                       "--microbatch-size 4 --num-microbatches 4 --device cpu --lr 1e-3 " + extra).split())
+    return build_global_config(args)
+
+
+def _oracle(cfg, P, batch):
+    """Full network with ordinary autograd; returns (loss, {stage: {name: grad}})."""
+    mods = []
+    for s in range(P):
+        set_seed(cfg.seed + s)
+        mods.append(build_stage_module(cfg, s, P, stage_kind(cfg)))
+    flats = [FlatParams(m, "cpu", want_shadow=False) for m in mods]
+    maths = [TorchMath(f, torch.float32, cfg.num_attention_heads) for f in flats]
+    eh0 = TorchEmbedHead(mods[0], flats[0], torch.float32)
+    ehl = TorchEmbedHead(mods[-1], flats[-1], torch.float32)
+    n = cfg.num_microbatches
+    ids = torch.chunk(batch["input_ids"], n)
+    tt = torch.chunk(batch["attention_mask"], n)
+    labels = torch.chunk(batch["labels"], n)
+    total = 0.0
+    for i in range(n):
+        x = eh0._embed((ids[i], tt[i]))
+        reversible = cfg.reversible
+        x2, x1 = x, x
+        for s in range(P):
+            for blk in mods[s].blocks:
+                if reversible:
+                    y1 = x1 + maths[s].attn(blk.F, x2).float()
+                    y2 = x2 + maths[s].mlp(blk.G, y1).float()
+                    x2, x1 = y2, y1
+                else:
+                    x2 = x2 + maths[s].attn(blk.F, x2).float()
+                    x2 = x2 + maths[s].mlp(blk.G, x2).float()
+        logits = ehl._head(x2, x1 if reversible else None)
+        total = total + Fn.cross_entropy(logits.float(), labels[i]) / n
+    total.backward()
+    grads = [{name: p.grad.clone() for name, p in m.named_parameters() if p.grad is not None} for m in mods]
+    return float(total), grads
+
+
+def _worker(rank, world, port, extra, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        cfg = _cfg(extra, world)
+        env = build_env(cfg, timeout_s=120)
+        set_seed(cfg.seed + rank)
+        tr = Trainer(cfg, env)
+        batch = SyntheticBatches(cfg, cfg.batch_size, 1, seed=123).make(0)
+        inputs = tr.split_inputs(batch) if tr.is_first else None
+        labels = batch["labels"] if tr.is_first else None
+        losses = tr.executor.step(inputs, labels, train=True)
+        grads = {name: g.clone() for name, g in tr.flat.named_grads()}
+        loss = float(torch.stack(losses).mean()) if tr.is_last else None
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (loss, grads))
+        tr.close()
+        if rank == 0:
+            q.put(("ok", gathered))
+        env.close()
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put(("err", f"rank {rank}: {traceback.format_exc()}"))
+        raise
+
+
+def _run(extra: str, world: int = 2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, extra, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    status, payload = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+    assert status == "ok", payload
+    return payload
+
+
+@pytest.mark.parametrize("extra", [
+    "--reversible",
+    "--reversible --schedule gpipe",
+    "--reversible --is_pareprop",
+    "--reversible --inverse",
+    "",
+    "--checkpointing",
+])
+def test_pipeline_matches_autograd(extra):
+    world = 2
+    gathered = _run(extra, world)
+    cfg = _cfg(extra, world)
+    batch = SyntheticBatches(cfg, cfg.batch_size, 1, seed=123).make(0)
+    ref_loss, ref_grads = _oracle(cfg, world, batch)
+    loss = gathered[-1][0]
+    assert abs(loss - ref_loss) <= 1e-5 * max(1.0, abs(ref_loss)), (loss, ref_loss)
+    for s in range(world):
+        got = gathered[s][1]
+        assert set(got) == set(ref_grads[s]), (sorted(got)[:5], sorted(ref_grads[s])[:5])
+        for name, g in got.items():
+            r = ref_grads[s][name]
+            err = (g - r).abs().max().item()
+            scale = r.abs().max().item()
+            assert err <= 1e-5 * max(scale, 1e-3), f"stage {s} {name}: err {err:.3e} scale {scale:.3e}"
+
+
+def test_four_stage_reversible():
+    gathered = _run("--reversible --num-hidden-layers 4", world=4)
+    cfg = _cfg("--reversible --num-hidden-layers 4", 4)
+    batch = SyntheticBatches(cfg, cfg.batch_size, 1, seed=123).make(0)
+    ref_loss, ref_grads = _oracle(cfg, 4, batch)
+    assert abs(gathered[-1][0] - ref_loss) <= 1e-5 * max(1.0, abs(ref_loss))
+    for s in range(4):
+        for name, g in gathered[s][1].items():
+            r = ref_grads[s][name]
+            assert (g - r).abs().max().item() <= 1e-5 * max(r.abs().max().item(), 1e-3), (s, name)
