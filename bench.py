@@ -1,0 +1,305 @@
+"""Training-throughput benchmark: reversible BERT-Large (24 x 1024, 16 heads, seq 512, bf16),
+pipeline-parallel over N GPUs (PP = N, 1F1B, one rank per GPU), global batch 512 in
+32 micro-batches of 16, synthetic data, random init.
+
+    python bench.py --gpus 1 --steps K --warmup W
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N --steps K --warmup W
+    ... --impl reference        # the reference implementation on the same config
+
+Reported (rank 0 prints one JSON line):
+  value  - samples/s of the whole job: global_batch / step time, where the step time is
+           K full training steps (pipeline forward/backward of every micro-batch, gradient
+           clipping, AdamW) timed with CUDA events between a barrier + synchronize on both
+           sides, the maximum over ranks.
+  e2e    - the same steps through Trainer.train_step with this step's inputs copied from
+           pinned host memory and the loss read back to the host every step, wall clock,
+           maximum over ranks.
+  peak_hbm_gib - max over ranks of torch.cuda.max_memory_allocated.
+  clocks - median SM clock and active throttle reasons sampled during the timed region.
+  gpu_launches - kernels launched by this framework's extension inside the timed region
+           (summed over ranks).
+The working set (fp32 weights + Adam state of the stage, activations of 16 x 512 x 1024
+micro-batches) is far larger than the 126 MB L2, so no flush is inserted between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "train samples/sec + peak HBM/GPU, Rev-BERT-Large PaBER at PP=1/2/4/8 vs ref"
+MODEL = dict(hidden=1024, heads=16, layers=24, seq=512, vocab=30522, classes=2)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["revpp", "reference"], default="revpp")
+    p.add_argument("--global-batch", type=int, default=512)
+    p.add_argument("--microbatch-size", type=int, default=16)
+    p.add_argument("--seq", type=int, default=MODEL["seq"])
+    p.add_argument("--layers", type=int, default=MODEL["layers"])
+    p.add_argument("--pareprop", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=900),
+                                device_id=dev)
+    return world, rank, local, dev
+
+
+def barrier(dev):
+    if dist.is_initialized():
+        dist.barrier(device_ids=[dev.index])
+
+
+def max_over_ranks(x: float, dev) -> float:
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, dev) -> float:
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def base_record(args, world, impl):
+    nmb = args.global_batch // args.microbatch_size
+    return {
+        "metric": METRIC, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform token ids, all-ones mask, Bernoulli labels), random init",
+        "impl": impl,
+        "config": {"model": "Rev-BERT-Large", "layers": args.layers, "hidden": MODEL["hidden"],
+                   "heads": MODEL["heads"], "global_batch": args.global_batch, "seq_len": args.seq,
+                   "microbatch_size": args.microbatch_size, "num_microbatches": nmb,
+                   "parallelism": f"pp{world}", "schedule": "1f1b",
+                   "backward": "pareprop" if args.pareprop else "sequential",
+                   "l2": "no flush: per-step working set (weights, Adam state, activations) >> 126 MB L2"},
+    }
+
+
+# ============================================================================ revpp arm
+def run_revpp(args):
+    sys.path.insert(0, HERE)
+    world, rank, local, dev = dist_setup(args.gpus)
+    from revpp.config import GlobalConfig, ParMode
+    from revpp.data import SyntheticBatches
+    from revpp.engine import Trainer
+    from revpp.ops import ext
+    from revpp.utils.clocks import ClockSampler
+    from revpp.utils.env import EnvContext
+    from revpp.utils.logger import build_logger
+    from revpp.utils.seed import set_seed
+
+    C = ext()
+    nmb = args.global_batch // args.microbatch_size
+    cfg = GlobalConfig(model="bert", par_mode=ParMode.PP if world > 1 else ParMode.NONE, reversible=True,
+                       is_pareprop=args.pareprop, num_hidden_layers=args.layers, hidden_size=MODEL["hidden"],
+                       num_attention_heads=MODEL["heads"], max_position_embeddings=args.seq, num_classes=2,
+                       autocast_dtype=torch.bfloat16, batch_size=args.global_batch,
+                       microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-4, dataset="synthetic")
+    lg = build_logger(f"bench{rank}", None)
+    env = EnvContext(world_size=world, rank=rank, local_rank=local, device=dev, proc_logger=lg, node_logger=None,
+                     main_logger=None, pg=dist.group.WORLD if dist.is_initialized() else None,
+                     master_rank=world - 1, num_stages=world, replicas=1)
+    set_seed(cfg.seed + rank)
+    tr = Trainer(cfg, env)
+    data = SyntheticBatches(cfg, args.global_batch, 4, seed=0)
+    batches = [data.make(i) for i in range(4)] if tr.is_first else [None] * 4
+
+    for i in range(args.warmup):
+        tr.train_step(batches[i % 4])
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+
+    # ---- device-timed region
+    sampler = ClockSampler(local)
+    barrier(dev)
+    torch.cuda.synchronize()
+    l0 = C.launch_count()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    last = None
+    for i in range(args.steps):
+        last = tr.train_step(batches[i % 4])
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier(dev)
+    launches = C.launch_count() - l0
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms, dev)
+    launches_total = sum_over_ranks(float(launches), dev)
+    peak = max_over_ranks(torch.cuda.max_memory_allocated() / 2**30, dev)
+    status = C.status_read_and_clear()
+
+    # ---- end-to-end: public API, H2D of each step's inputs, D2H of each step's loss
+    e2e = None
+    if not args.no_e2e:
+        h2d = sum(t.numel() * t.element_size() for t in batches[0].values()) if tr.is_first else 0
+        barrier(dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            loss = tr.train_step(batches[i % 4])
+            if loss is not None:
+                float(loss)  # device -> host read of the step's result
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3 / args.steps
+        barrier(dev)
+        wall_max = max_over_ranks(wall, dev)
+        h2d_total = sum_over_ranks(float(h2d), dev)
+        e2e = {"value": args.global_batch / (wall_max / 1e3), "unit": "samples/s", "ms_per_step": wall_max,
+               "h2d_bytes_per_step": int(h2d_total), "d2h_bytes_per_step": 4,
+               "api": "revpp.engine.Trainer.train_step"}
+    loss_val = float(last) if last is not None else None
+    tr.close()
+    rec = base_record(args, world, "revpp")
+    rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "e2e": e2e,
+                "gpu_launches": int(launches_total), "peak_hbm_gib": peak, "clocks": clocks,
+                "device_status": status})
+    if loss_val is not None:
+        rec["final_loss"] = loss_val
+    # the loss lives on the last rank; rank 0 prints
+    if dist.is_initialized():
+        obj = [rec.get("final_loss")]
+        dist.broadcast_object_list(obj, src=world - 1)
+        rec["final_loss"] = obj[0]
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if dist.is_initialized():
+        barrier(dev)
+        dist.destroy_process_group()
+
+
+# ============================================================================ reference arm
+REF_ROOT = os.path.join(HERE, "baseline", "_ref", "BERT")
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if not os.path.isdir(REF_ROOT):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
+        return
+    if world < 2:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference cannot train reversible BERT on one GPU: PP=1 builds a first stage "
+                              "without a head (BERT/experiment/base.py:166) and its non-PP reversible model "
+                              "computes no body gradients (BERT/models/reversible.py:125)"}), flush=True)
+        return
+    world, rank, local, dev = dist_setup(args.gpus)
+    sys.path.insert(0, REF_ROOT)
+    from models.bert_stages import BertFirstStage, BertLastStage, BertMidStage  # noqa: E402
+    from pipelining import RevPipelineStageWithPareprop, Schedule1F1B  # noqa: E402
+
+    from revpp.utils.clocks import ClockSampler  # timing helper only
+
+    torch.manual_seed(rank)
+    nmb = args.global_batch // args.microbatch_size
+    kw = dict(hidden_size=MODEL["hidden"], num_attention_heads=MODEL["heads"], num_blocks=args.layers // world,
+              enable_amp=True, autocast_dtype=torch.bfloat16, is_pareprop=args.pareprop)
+    if rank == 0:
+        model = BertFirstStage(vocab_size=MODEL["vocab"], max_position_embeddings=args.seq, type_vocab_size=2, **kw)
+    elif rank == world - 1:
+        model = BertLastStage(num_classes=MODEL["classes"], **kw)
+    else:
+        model = BertMidStage(**kw)
+    model = model.to(dev)
+    stage = RevPipelineStageWithPareprop(submodule=model, stage_index=rank, num_stages=world, device=dev)
+    sched = Schedule1F1B(stage=stage, n_microbatches=nmb, loss_fn=torch.nn.CrossEntropyLoss())
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, eps=1e-6)
+    g = torch.Generator().manual_seed(0)
+    B, S = args.global_batch, args.seq
+    host = [dict(ids=torch.randint(0, MODEL["vocab"], (B, S), generator=g).pin_memory(),
+                 mask=torch.ones(B, S, dtype=torch.int64).pin_memory(),
+                 labels=torch.bernoulli(torch.full((B,), 0.5), generator=g).long().pin_memory()) for _ in range(2)]
+    labels_buf = torch.zeros(B, dtype=torch.int64, device=dev)
+
+    def step(i):
+        # the loop body of the reference Engine (BERT/src/engine.py:160-281); its own loop
+        # deletes an unbound name after the first batch on rank 0 (engine.py:197).
+        b = host[i % 2]
+        if rank == 0:
+            ids = b["ids"].to(dev, non_blocking=True)
+            mask = b["mask"].to(dev, non_blocking=True)
+            lab = b["labels"].to(dev, non_blocking=True)
+            dist.isend(lab, dst=world - 1).wait()
+            sched.step(ids, mask)
+        elif rank == world - 1:
+            dist.irecv(labels_buf, src=0).wait()
+            losses = []
+            sched.step(target=labels_buf, losses=losses)
+        else:
+            sched.step()
+        for p in model.parameters():
+            if p.grad is not None:
+                p.grad.div_(nmb)
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        opt.zero_grad()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    sampler = ClockSampler(local)
+    barrier(dev)
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier(dev)
+    ms_max = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    peak = max_over_ranks(torch.cuda.max_memory_allocated() / 2**30, dev)
+    rec = base_record(args, world, "reference")
+    rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "peak_hbm_gib": peak,
+                "clocks": clocks, "gpu_launches": 0,
+                "api": "pipelining.RevPipelineStageWithPareprop + Schedule1F1B (baseline/_ref/BERT)"})
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    barrier(dev)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_revpp(a)

@@ -43,6 +43,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_peek", &revpp::status_peek, "Read the device error word of the current device");
   m.def("status_read_and_clear", &revpp::status_read_and_clear, "Read and clear the device error word");
   m.def("num_sms", &revpp::num_sms);
+  m.def("launch_count", &revpp::launch_count, "kernels launched by this process through the extension");
   m.def("set_sm_reserve", &revpp::set_sm_reserve, "SMs left free of persistent GEMM CTAs");
   m.def("sm_reserve", &revpp::sm_reserve);
   m.def("grad_sumsq", &revpp::grad_sumsq, py::arg("g"), py::arg("out"));

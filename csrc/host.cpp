@@ -3,6 +3,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 namespace revpp {
@@ -66,7 +67,10 @@ int status_read_and_clear() {
 
 namespace {
 int g_sm_reserve = 0;
+std::atomic<int64_t> g_launches{0};
 }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 void set_sm_reserve(int n) { g_sm_reserve = n < 0 ? 0 : n; }
 int sm_reserve() { return g_sm_reserve; }
 

@@ -28,9 +28,17 @@
     REVPP_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " (", #expr, ")");         \
   } while (0)
 
-#define REVPP_CHECK_LAUNCH() REVPP_CUDA_CHECK(cudaGetLastError())
+#define REVPP_CHECK_LAUNCH()               \
+  do {                                     \
+    REVPP_CUDA_CHECK(cudaGetLastError());  \
+    ::revpp::count_launch();               \
+  } while (0)
 
 namespace revpp {
+
+// Number of kernels this process has launched through the extension.
+void count_launch();
+int64_t launch_count();
 
 // Device pointer of this process's status word for the current device.  Kernels
 // OR error bits into it; the host reads it through the mapped pinned page

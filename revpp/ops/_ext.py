@@ -5,6 +5,8 @@ machine every op raises instead of silently falling back to PyTorch.
 """
 from __future__ import annotations
 
+import torch  # noqa: F401  (loads libc10 / libtorch before the extension)
+
 _C = None
 _ERR: Exception | None = None
 

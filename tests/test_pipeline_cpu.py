@@ -92,7 +92,9 @@ def _worker(rank, world, port, extra, q):
         dist.all_gather_object(gathered, (loss, grads))
         tr.close()
         if rank == 0:
-            q.put(("ok", gathered))
+            # numpy arrays pickle by value (tensors would go through shared-memory handles
+            # that die with this process)
+            q.put(("ok", [(l, {k: v.numpy() for k, v in g.items()}) for l, g in gathered]))
         env.close()
     except Exception as e:  # noqa: BLE001
         import traceback
@@ -112,7 +114,7 @@ def _run(extra: str, world: int = 2):
     for p in procs:
         p.join(timeout=120)
     assert status == "ok", payload
-    return payload
+    return [(l, {k: torch.from_numpy(v) for k, v in g.items()}) for l, g in payload]
 
 
 @pytest.mark.parametrize("extra", [
