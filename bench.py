@@ -124,7 +124,7 @@ def run_revpp(args):
                        is_pareprop=args.pareprop, num_hidden_layers=args.layers, hidden_size=MODEL["hidden"],
                        num_attention_heads=MODEL["heads"], max_position_embeddings=args.seq, num_classes=2,
                        autocast_dtype=torch.bfloat16, batch_size=args.global_batch,
-                       microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-4, dataset="synthetic")
+                       microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-5, dataset="synthetic")
     lg = build_logger(f"bench{rank}", None)
     env = EnvContext(world_size=world, rank=rank, local_rank=local, device=dev, proc_logger=lg, node_logger=None,
                      main_logger=None, pg=dist.group.WORLD if dist.is_initialized() else None,
@@ -238,7 +238,7 @@ def run_reference(args):
     model = model.to(dev)
     stage = RevPipelineStageWithPareprop(submodule=model, stage_index=rank, num_stages=world, device=dev)
     sched = Schedule1F1B(stage=stage, n_microbatches=nmb, loss_fn=torch.nn.CrossEntropyLoss())
-    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, eps=1e-6)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-5, weight_decay=0.01, eps=1e-6)
     g = torch.Generator().manual_seed(0)
     B, S = args.global_batch, args.seq
     host = [dict(ids=torch.randint(0, MODEL["vocab"], (B, S), generator=g).pin_memory(),

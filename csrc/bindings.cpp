@@ -33,6 +33,31 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
                 double wd, int64_t step, double max_norm, const c10::optional<torch::Tensor>& sumsq,
                 bool zero_grad);
 void scale_(torch::Tensor x, double s);
+// embed_head.cu
+void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
+                    const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
+                    const torch::Tensor& beta, double eps, torch::Tensor out);
+void bert_embed_bwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
+                    const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma, double eps,
+                    const torch::Tensor& dx2, const c10::optional<torch::Tensor>& dx1, torch::Tensor dword,
+                    torch::Tensor dpos, torch::Tensor dtype, torch::Tensor dgamma, torch::Tensor dbeta);
+void im2col_patches(const torch::Tensor& img, int64_t patch, torch::Tensor out);
+void vit_assemble_fwd(const torch::Tensor& conv, const torch::Tensor& cls, const torch::Tensor& pos,
+                      const torch::Tensor& gamma, const torch::Tensor& beta, double eps, int64_t B, int64_t S,
+                      torch::Tensor out);
+void vit_assemble_bwd(const torch::Tensor& conv, const torch::Tensor& cls, const torch::Tensor& pos,
+                      const torch::Tensor& gamma, double eps, int64_t B, int64_t S, const torch::Tensor& dx2,
+                      const c10::optional<torch::Tensor>& dx1, torch::Tensor dconv, torch::Tensor dcls,
+                      torch::Tensor dpos, torch::Tensor dgamma, torch::Tensor dbeta);
+void head_fwd_bwd(const torch::Tensor& y2, const c10::optional<torch::Tensor>& y1, int64_t mode,
+                  const torch::Tensor& gamma, const torch::Tensor& beta, double eps, const torch::Tensor& wb,
+                  const torch::Tensor& bb, const c10::optional<torch::Tensor>& labels, double grad_scale,
+                  torch::Tensor pooled, torch::Tensor logits, torch::Tensor loss, bool want_grad,
+                  const c10::optional<torch::Tensor>& dlogits, const c10::optional<torch::Tensor>& hb,
+                  const c10::optional<torch::Tensor>& dpooled, const c10::optional<torch::Tensor>& dW,
+                  const c10::optional<torch::Tensor>& db, const c10::optional<torch::Tensor>& dgamma,
+                  const c10::optional<torch::Tensor>& dbeta, const c10::optional<torch::Tensor>& dy2,
+                  const c10::optional<torch::Tensor>& dy1);
 // host.cpp
 void set_sm_reserve(int n);
 int sm_reserve();
@@ -69,6 +94,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("heads"));
   m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
         py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
+  m.def("bert_embed_fwd", &revpp::bert_embed_fwd);
+  m.def("bert_embed_bwd", &revpp::bert_embed_bwd, py::arg("ids"), py::arg("tt"), py::arg("word"), py::arg("pos"),
+        py::arg("type"), py::arg("gamma"), py::arg("eps"), py::arg("dx2"), py::arg("dx1"), py::arg("dword"),
+        py::arg("dpos"), py::arg("dtype"), py::arg("dgamma"), py::arg("dbeta"));
+  m.def("im2col_patches", &revpp::im2col_patches);
+  m.def("vit_assemble_fwd", &revpp::vit_assemble_fwd);
+  m.def("vit_assemble_bwd", &revpp::vit_assemble_bwd, py::arg("conv"), py::arg("cls"), py::arg("pos"),
+        py::arg("gamma"), py::arg("eps"), py::arg("B"), py::arg("S"), py::arg("dx2"), py::arg("dx1"),
+        py::arg("dconv"), py::arg("dcls"), py::arg("dpos"), py::arg("dgamma"), py::arg("dbeta"));
+  m.def("head_fwd_bwd", &revpp::head_fwd_bwd, py::arg("y2"), py::arg("y1"), py::arg("mode"), py::arg("gamma"),
+        py::arg("beta"), py::arg("eps"), py::arg("wb"), py::arg("bb"), py::arg("labels"), py::arg("grad_scale"),
+        py::arg("pooled"), py::arg("logits"), py::arg("loss"), py::arg("want_grad"), py::arg("dlogits") = py::none(),
+        py::arg("hb") = py::none(), py::arg("dpooled") = py::none(), py::arg("dW") = py::none(),
+        py::arg("db") = py::none(), py::arg("dgamma") = py::none(), py::arg("dbeta") = py::none(),
+        py::arg("dy2") = py::none(), py::arg("dy1") = py::none());
   m.def("cast_colsum", &revpp::cast_colsum, py::arg("inp"), py::arg("out") = py::none(),
         py::arg("colsum") = py::none());
 }

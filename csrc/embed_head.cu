@@ -1,0 +1,689 @@
+// Embedding, patch-embedding and classifier-head kernels.
+//
+// BERT embedding (BERT/models/bert_blocks.py:9-31):
+//   fwd: x[t] = LN_1e-5(word[id[t]] + pos[t % S] + type[tt[t]])                 fp32 out
+//   bwd: recompute the pre-LN sum, LN backward of dx = dX2 + dX1 (the coupling
+//        duplicates x), scatter into the word table (padding row 0 skipped), and per
+//        position / per type / gamma / beta sums.  One CTA per position owns dpos[s].
+// ViT patch embedding (Vit/models/vit_blocks.py:42-62), conv k = s = p as a GEMM:
+//   im2col : images fp32 NCHW -> patches bf16 [B*np, C*p*p] (c, kh, kw order = conv weight)
+//   GEMM   : conv = patches @ W^T + b  (tcgen05 GEMM, bf16 out as under autocast)
+//   assemble fwd: x[b,0] = LN(cls + pos[0]), x[b,1+i] = LN(conv[b,i] + pos[1+i])
+//   assemble bwd: LN backward; dcls, dpos sums; dconv (bf16) for the weight-gradient GEMM
+// Classifier head (BERT/models/bert_stages.py:436-444, Vit/models/vit_stages.py:410-419):
+//   pool   : z = decouple(Y2, Y1) (sum, or concat [Y1, Y2] for the inverse variant),
+//            mean over the sequence or the CLS row
+//   head   : h = LN(pooled); logits = bf16(bf16(h) W^T + b); CE in fp32; dlogits scaled
+//            by grad_scale / batch; dh = dlogits W; LN backward -> dpooled
+//   wgrad  : dW += dlogits^T bf16(h), db += sum(dlogits)
+//   spread : dY = dpooled / S on every row (mean) or on row 0 (CLS)
+#include "common.cuh"
+#include "host.h"
+
+namespace revpp {
+
+namespace {
+constexpr int kWarps = 8;
+
+template <int VPL>
+__device__ __forceinline__ void row_stats(const float4 (&v)[VPL], float& mean, float& rstd, float eps) {
+  constexpr int H = VPL * 128;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) s += v[i].x + v[i].y + v[i].z + v[i].w;
+  mean = warp_sum(s) * (1.0f / H);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    ss += a * a + b * b + c * c + d * d;
+  }
+  rstd = rsqrtf(warp_sum(ss) * (1.0f / H) + eps);
+}
+
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+}  // namespace
+
+// ------------------------------------------------------------------ BERT embedding
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+    bert_embed_fwd_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ tt,
+                          const float* __restrict__ word, const float* __restrict__ pos,
+                          const float* __restrict__ type, const float* __restrict__ gamma,
+                          const float* __restrict__ beta, float eps, int M, int S, int V, int T,
+                          float* __restrict__ out, int* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= M) return;
+  constexpr int H = VPL * 128;
+  long long id = ids[row];
+  long long ty = tt[row];
+  if (id < 0 || id >= V || ty < 0 || ty >= T) {  // out-of-range token: record and embed zero
+    if (lane == 0) atomicOr(status, kStatusBadShape);
+    id = id < 0 || id >= V ? 0 : id;
+    ty = ty < 0 || ty >= T ? 0 : ty;
+  }
+  const int s = row % S;
+  const float4* w4 = reinterpret_cast<const float4*>(word + id * H);
+  const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
+  const float4* t4 = reinterpret_cast<const float4*>(type + ty * H);
+  float4 v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) v[i] = f4add(f4add(__ldg(w4 + lane + 32 * i), __ldg(p4 + lane + 32 * i)), __ldg(t4 + lane + 32 * i));
+  float mean, rstd;
+  row_stats<VPL>(v, mean, rstd, eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  float4* o4 = reinterpret_cast<float4*>(out + static_cast<long long>(row) * H);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const float4 g = __ldg(g4 + c), b = __ldg(b4 + c);
+    o4[c] = make_float4((v[i].x - mean) * rstd * g.x + b.x, (v[i].y - mean) * rstd * g.y + b.y,
+                        (v[i].z - mean) * rstd * g.z + b.z, (v[i].w - mean) * rstd * g.w + b.w);
+  }
+}
+
+// grid = S (one CTA per position), CTA loops over the batch.
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+    bert_embed_bwd_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ tt,
+                          const float* __restrict__ word, const float* __restrict__ pos,
+                          const float* __restrict__ type, const float* __restrict__ gamma, float eps, int B, int S,
+                          int V, int T, const float* __restrict__ dx2, const float* __restrict__ dx1,
+                          float* __restrict__ dword, float* __restrict__ dpos, float* __restrict__ dtype,
+                          float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  constexpr int H = VPL * 128;
+  extern __shared__ float sacc[];  // [4 + T][H]: dpos, dgamma, dbeta, spare, dtype[T]
+  for (int i = threadIdx.x; i < (4 + T) * H; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int s = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  for (int b = warp; b < B; b += kWarps) {
+    const long long row = static_cast<long long>(b) * S + s;
+    long long id = ids[row], ty = tt[row];
+    id = id < 0 || id >= V ? 0 : id;
+    ty = ty < 0 || ty >= T ? 0 : ty;
+    const float4* w4 = reinterpret_cast<const float4*>(word + id * H);
+    const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
+    const float4* t4 = reinterpret_cast<const float4*>(type + ty * H);
+    float4 v[VPL], dy[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = f4add(f4add(__ldg(w4 + c), __ldg(p4 + c)), __ldg(t4 + c));
+      dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
+      if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
+    }
+    float mean, rstd;
+    row_stats<VPL>(v, mean, rstd, eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float4 g = __ldg(g4 + lane + 32 * i);
+      v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
+      s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
+      s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
+    }
+    const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
+    float* wrow = dword + id * H;
+    float* trow = sacc + (4 + ty) * H;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      const float4 g = __ldg(g4 + lane + 32 * i);
+      const float dv[4] = {rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
+                           rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2)};
+      const float dyv[4] = {dy[i].x, dy[i].y, dy[i].z, dy[i].w};
+      const float xh[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      if (id != 0) atomicAdd(reinterpret_cast<float4*>(wrow + c), make_float4(dv[0], dv[1], dv[2], dv[3]));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        atomicAdd(&sacc[0 * H + c + j], dv[j]);
+        atomicAdd(&sacc[1 * H + c + j], dyv[j] * xh[j]);
+        atomicAdd(&sacc[2 * H + c + j], dyv[j]);
+        atomicAdd(&trow[c + j], dv[j]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    dpos[static_cast<long long>(s) * H + c] += sacc[c];  // this CTA owns row s
+    atomicAdd(dgamma + c, sacc[H + c]);
+    atomicAdd(dbeta + c, sacc[2 * H + c]);
+    for (int t = 0; t < T; ++t) {
+      const float v = sacc[(4 + t) * H + c];
+      if (v != 0.f) atomicAdd(dtype + static_cast<long long>(t) * H + c, v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ ViT patch embedding
+// patches[b*np + py*g + px, c*p*p + kh*p + kw] = bf16(img[b, c, py*p + kh, px*p + kw])
+__global__ void im2col_patches_kernel(const float* __restrict__ img, __nv_bfloat16* __restrict__ out, int B, int C,
+                                      int I, int p) {
+  const int g = I / p, np = g * g, K = C * p * p;
+  const long long total = static_cast<long long>(B) * np * K;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(e % K);
+    const long long r = e / K;
+    const int patch = static_cast<int>(r % np);
+    const int b = static_cast<int>(r / np);
+    const int c = k / (p * p), kh = (k / p) % p, kw = k % p;
+    const int y = (patch / g) * p + kh, x = (patch % g) * p + kw;
+    out[e] = __float2bfloat16_rn(img[((static_cast<long long>(b) * C + c) * I + y) * I + x]);
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+    vit_assemble_fwd_kernel(const __nv_bfloat16* __restrict__ conv, const float* __restrict__ cls,
+                            const float* __restrict__ pos, const float* __restrict__ gamma,
+                            const float* __restrict__ beta, float eps, int B, int S, float* __restrict__ out) {
+  constexpr int H = VPL * 128;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= B * S) return;
+  const int b = row / S, s = row % S;
+  float4 v[VPL];
+  const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    float4 a;
+    if (s == 0) {
+      a = __ldg(reinterpret_cast<const float4*>(cls) + c);
+    } else {
+      const uint2 q = *reinterpret_cast<const uint2*>(conv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + 4 * c);
+      const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
+      a = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    v[i] = f4add(a, __ldg(p4 + c));
+  }
+  float mean, rstd;
+  row_stats<VPL>(v, mean, rstd, eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  float4* o4 = reinterpret_cast<float4*>(out + static_cast<long long>(row) * H);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const float4 g = __ldg(g4 + c), bb = __ldg(b4 + c);
+    o4[c] = make_float4((v[i].x - mean) * rstd * g.x + bb.x, (v[i].y - mean) * rstd * g.y + bb.y,
+                        (v[i].z - mean) * rstd * g.z + bb.z, (v[i].w - mean) * rstd * g.w + bb.w);
+  }
+}
+
+// grid = S (one CTA per token position), loops over the batch.
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+    vit_assemble_bwd_kernel(const __nv_bfloat16* __restrict__ conv, const float* __restrict__ cls,
+                            const float* __restrict__ pos, const float* __restrict__ gamma, float eps, int B, int S,
+                            const float* __restrict__ dx2, const float* __restrict__ dx1,
+                            __nv_bfloat16* __restrict__ dconv, float* __restrict__ dcls, float* __restrict__ dpos,
+                            float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  constexpr int H = VPL * 128;
+  extern __shared__ float sacc[];  // [3][H]: dpos, dgamma, dbeta
+  for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int s = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
+  for (int b = warp; b < B; b += kWarps) {
+    const long long row = static_cast<long long>(b) * S + s;
+    float4 v[VPL], dy[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      float4 a;
+      if (s == 0) {
+        a = __ldg(reinterpret_cast<const float4*>(cls) + c);
+      } else {
+        const uint2 q = *reinterpret_cast<const uint2*>(conv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + 4 * c);
+        const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
+        a = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+      v[i] = f4add(a, __ldg(p4 + c));
+      dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
+      if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
+    }
+    float mean, rstd;
+    row_stats<VPL>(v, mean, rstd, eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float4 g = __ldg(g4 + lane + 32 * i);
+      v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
+      s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
+      s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
+    }
+    const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      const float4 g = __ldg(g4 + lane + 32 * i);
+      const float dv[4] = {rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
+                           rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2)};
+      const float dyv[4] = {dy[i].x, dy[i].y, dy[i].z, dy[i].w};
+      const float xh[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      if (s > 0) {
+        *reinterpret_cast<uint2*>(dconv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + c) =
+            make_uint2(pack_bf16x2(dv[0], dv[1]), pack_bf16x2(dv[2], dv[3]));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        atomicAdd(&sacc[c + j], dv[j]);
+        atomicAdd(&sacc[H + c + j], dyv[j] * xh[j]);
+        atomicAdd(&sacc[2 * H + c + j], dyv[j]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    dpos[static_cast<long long>(s) * H + c] += sacc[c];
+    if (s == 0) dcls[c] += sacc[c];
+    atomicAdd(dgamma + c, sacc[H + c]);
+    atomicAdd(dbeta + c, sacc[2 * H + c]);
+  }
+}
+
+// ------------------------------------------------------------------ head
+// pooled[b, :] : mode 0 mean over S of (y2 + y1); mode 1 row 0 of (y2 + y1);
+//                mode 2 row 0 of concat [y1, y2] (width 2H); y1 may be null (single stream).
+__global__ void head_pool_kernel(const float* __restrict__ y2, const float* __restrict__ y1, int B, int S, int H,
+                                 int mode, float* __restrict__ pooled) {
+  const int b = blockIdx.y;
+  const int W = mode == 2 ? 2 * H : H;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= W) return;
+  const long long base = static_cast<long long>(b) * S * H;
+  float acc = 0.f;
+  if (mode == 0) {
+    for (int s = 0; s < S; ++s) {
+      acc += y2[base + static_cast<long long>(s) * H + c];
+      if (y1) acc += y1[base + static_cast<long long>(s) * H + c];
+    }
+    acc *= 1.0f / S;
+  } else if (mode == 1) {
+    acc = y2[base + c] + (y1 ? y1[base + c] : 0.f);
+  } else {
+    acc = c < H ? y1[base + c] : y2[base + c - H];
+  }
+  pooled[static_cast<long long>(b) * W + c] = acc;
+}
+
+// One CTA per sample.  smem: h[W], dh[W], logits[C].
+__global__ void head_fwd_bwd_kernel(const float* __restrict__ pooled, int W, const float* __restrict__ gamma,
+                                    const float* __restrict__ beta, float eps, const __nv_bfloat16* __restrict__ wb,
+                                    const __nv_bfloat16* __restrict__ bb, int C, const int64_t* __restrict__ labels,
+                                    float grad_scale, int B, float* __restrict__ logits_out,
+                                    float* __restrict__ loss_out, float* __restrict__ dlogits,
+                                    __nv_bfloat16* __restrict__ hb_out, float* __restrict__ dpooled,
+                                    float* __restrict__ dgamma, float* __restrict__ dbeta, int want_grad,
+                                    int* __restrict__ status) {
+  extern __shared__ float sm[];
+  float* h = sm;            // normalised (pre-affine) x-hat
+  float* y = sm + W;        // LN output (bf16-rounded, the GEMM operand)
+  float* lg = sm + 2 * W;   // logits / probabilities
+  float* red = lg + C;      // 64 floats of reduction scratch
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+  const float* x = pooled + static_cast<long long>(b) * W;
+  // LN statistics
+  float s = 0.f;
+  for (int i = tid; i < W; i += nt) s += x[i];
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? red[lane] : 0.f;
+    v = warp_sum(v);
+    if (lane == 0) red[32] = v / W;
+  }
+  __syncthreads();
+  const float mean = red[32];
+  float ss = 0.f;
+  for (int i = tid; i < W; i += nt) {
+    const float d = x[i] - mean;
+    ss += d * d;
+  }
+  ss = warp_sum(ss);
+  __syncthreads();
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? red[lane] : 0.f;
+    v = warp_sum(v);
+    if (lane == 0) red[33] = rsqrtf(v / W + eps);
+  }
+  __syncthreads();
+  const float rstd = red[33];
+  for (int i = tid; i < W; i += nt) {
+    const float xh = (x[i] - mean) * rstd;
+    h[i] = xh;
+    y[i] = bf16r(xh * gamma[i] + beta[i]);
+    if (hb_out) hb_out[static_cast<long long>(b) * W + i] = __float2bfloat16_rn(y[i]);
+  }
+  __syncthreads();
+  // logits: one warp per class
+  for (int c = warp; c < C; c += nw) {
+    const __nv_bfloat16* wr = wb + static_cast<long long>(c) * W;
+    float acc = 0.f;
+    for (int i = lane; i < W; i += 32) acc += __bfloat162float(wr[i]) * y[i];
+    acc = warp_sum(acc);
+    if (lane == 0) lg[c] = bf16r(acc + __bfloat162float(bb[c]));
+  }
+  __syncthreads();
+  // softmax / CE
+  float mx = -INFINITY;
+  for (int c = tid; c < C; c += nt) mx = fmaxf(mx, lg[c]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? red[lane] : -INFINITY;
+    v = warp_max(v);
+    if (lane == 0) red[34] = v;
+  }
+  __syncthreads();
+  mx = red[34];
+  float se = 0.f;
+  for (int c = tid; c < C; c += nt) se += expf(lg[c] - mx);
+  se = warp_sum(se);
+  __syncthreads();
+  if (lane == 0) red[warp] = se;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < nw ? red[lane] : 0.f;
+    v = warp_sum(v);
+    if (lane == 0) red[35] = v;
+  }
+  __syncthreads();
+  const float lse = mx + logf(red[35]);
+  long long lab = labels ? labels[b] : 0;
+  if (lab < 0 || lab >= C) {
+    if (tid == 0 && status) atomicOr(status, kStatusBadShape);
+    lab = 0;
+  }
+  if (tid == 0 && loss_out) loss_out[b] = lse - lg[lab];
+  for (int c = tid; c < C; c += nt) {
+    if (logits_out) logits_out[static_cast<long long>(b) * C + c] = lg[c];
+  }
+  if (!want_grad) return;
+  __syncthreads();
+  const float sc = grad_scale / B;
+  for (int c = tid; c < C; c += nt) {
+    const float p = expf(lg[c] - lse);
+    const float d = (p - (c == lab ? 1.f : 0.f)) * sc;
+    lg[c] = d;
+    dlogits[static_cast<long long>(b) * C + c] = d;
+  }
+  __syncthreads();
+  // dy = dlogits @ W (bf16 operands); LN backward
+  float a1 = 0.f, a2 = 0.f;
+  for (int i = tid; i < W; i += nt) {
+    float acc = 0.f;
+    for (int c = 0; c < C; ++c) acc += bf16r(lg[c]) * __bfloat162float(wb[static_cast<long long>(c) * W + i]);
+    const float g = acc * gamma[i];
+    y[i] = acc;  // reuse as dy
+    a1 += g;
+    a2 += g * h[i];
+    atomicAdd(dgamma + i, acc * h[i]);
+    atomicAdd(dbeta + i, acc);
+  }
+  a1 = warp_sum(a1);
+  a2 = warp_sum(a2);
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = a1;
+    red[32 + warp] = a2;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float u = lane < nw ? red[lane] : 0.f, v = lane < nw ? red[32 + lane] : 0.f;
+    u = warp_sum(u);
+    v = warp_sum(v);
+    if (lane == 0) {
+      red[40] = u / W;
+      red[41] = v / W;
+    }
+  }
+  __syncthreads();
+  const float m1 = red[40], m2 = red[41];
+  for (int i = tid; i < W; i += nt) {
+    dpooled[static_cast<long long>(b) * W + i] = rstd * (y[i] * gamma[i] - m1 - h[i] * m2);
+  }
+}
+
+// dW[c, i] += sum_b bf16(dlogits[b, c]) * hb[b, i];  db[c] += sum_b dlogits[b, c]
+__global__ void head_wgrad_kernel(const float* __restrict__ dlogits, const __nv_bfloat16* __restrict__ hb, int B,
+                                  int C, int W, float* __restrict__ dW, float* __restrict__ db) {
+  const long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (e >= static_cast<long long>(C) * W) return;
+  const int c = static_cast<int>(e / W), i = static_cast<int>(e % W);
+  float acc = 0.f, accb = 0.f;
+  for (int b = 0; b < B; ++b) {
+    const float d = dlogits[static_cast<long long>(b) * C + c];
+    acc += bf16r(d) * __bfloat162float(hb[static_cast<long long>(b) * W + i]);
+    accb += d;
+  }
+  dW[e] += acc;
+  if (i == 0) db[c] += accb;
+}
+
+// dY[b, s, :] from dpooled[b, :]: mode 0 -> dpooled / S on every row, mode 1 -> row 0 only,
+// mode 2 (concat) -> dy1 = first half, dy2 = second half, row 0 only.
+__global__ void head_spread_kernel(const float* __restrict__ dpooled, int B, int S, int H, int mode,
+                                   float* __restrict__ dy2, float* __restrict__ dy1) {
+  const long long n4 = static_cast<long long>(B) * S * H / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long e = i * 4;
+    const int c = static_cast<int>(e % H);
+    const long long r = e / H;
+    const int s = static_cast<int>(r % S), b = static_cast<int>(r / S);
+    float4 v2 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v2;
+    if (mode == 0) {
+      const float4 p = *reinterpret_cast<const float4*>(dpooled + static_cast<long long>(b) * H + c);
+      const float inv = 1.0f / S;
+      v2 = make_float4(p.x * inv, p.y * inv, p.z * inv, p.w * inv);
+      v1 = v2;
+    } else if (s == 0) {
+      if (mode == 1) {
+        v2 = *reinterpret_cast<const float4*>(dpooled + static_cast<long long>(b) * H + c);
+        v1 = v2;
+      } else {
+        v1 = *reinterpret_cast<const float4*>(dpooled + static_cast<long long>(b) * 2 * H + c);
+        v2 = *reinterpret_cast<const float4*>(dpooled + static_cast<long long>(b) * 2 * H + H + c);
+      }
+    }
+    reinterpret_cast<float4*>(dy2)[i] = v2;
+    if (dy1) reinterpret_cast<float4*>(dy1)[i] = v1;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+template <typename F>
+void vpl_dispatch(int H, F&& f) {
+  REVPP_CHECK(H % 128 == 0 && H >= 128 && H <= 2048, "width must be a multiple of 128 in [128, 2048], got ", H);
+  switch (H / 128) {
+    case 1: f(std::integral_constant<int, 1>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}); break;
+    case 6: f(std::integral_constant<int, 6>{}); break;
+    case 8: f(std::integral_constant<int, 8>{}); break;
+    case 12: f(std::integral_constant<int, 12>{}); break;
+    case 16: f(std::integral_constant<int, 16>{}); break;
+    default: REVPP_CHECK(false, "unsupported width ", H);
+  }
+}
+int grid1d(long long n, int threads) {
+  return static_cast<int>(std::max<long long>(1, std::min<long long>((n + threads - 1) / threads, 16LL * num_sms())));
+}
+}  // namespace
+
+void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
+                    const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
+                    const torch::Tensor& beta, double eps, torch::Tensor out) {
+  REVPP_CHECK(ids.scalar_type() == at::kLong && tt.scalar_type() == at::kLong, "ids must be int64");
+  REVPP_CHECK(ids.is_contiguous() && tt.is_contiguous() && ids.sizes() == tt.sizes() && ids.dim() == 2, "ids [B, S]");
+  check_cuda_f32(out, "out");
+  const int B = static_cast<int>(ids.size(0)), S = static_cast<int>(ids.size(1));
+  const int H = static_cast<int>(word.size(1));
+  REVPP_CHECK(pos.size(0) >= S, "sequence longer than the position table");
+  c10::cuda::CUDAGuard guard(ids.device());
+  const int M = B * S;
+  vpl_dispatch(H, [&](auto v) {
+    bert_embed_fwd_kernel<decltype(v)::value><<<(M + kWarps - 1) / kWarps, kWarps * 32, 0, cur_stream()>>>(
+        ids.data_ptr<int64_t>(), tt.data_ptr<int64_t>(), word.data_ptr<float>(), pos.data_ptr<float>(),
+        type.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(), static_cast<float>(eps), M, S,
+        static_cast<int>(word.size(0)), static_cast<int>(type.size(0)), out.data_ptr<float>(), status_device_ptr());
+  });
+  REVPP_CHECK_LAUNCH();
+}
+
+void bert_embed_bwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
+                    const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma, double eps,
+                    const torch::Tensor& dx2, const c10::optional<torch::Tensor>& dx1, torch::Tensor dword,
+                    torch::Tensor dpos, torch::Tensor dtype, torch::Tensor dgamma, torch::Tensor dbeta) {
+  const int B = static_cast<int>(ids.size(0)), S = static_cast<int>(ids.size(1));
+  const int H = static_cast<int>(word.size(1));
+  const int T = static_cast<int>(type.size(0));
+  check_cuda_f32(dx2, "dx2");
+  REVPP_CHECK(dx2.is_contiguous() && dx2.numel() == static_cast<long long>(B) * S * H, "dx2 [B, S, H]");
+  const float* d1 = nullptr;
+  if (dx1.has_value() && dx1->defined()) {
+    REVPP_CHECK(dx1->is_contiguous() && dx1->numel() == dx2.numel(), "dx1 [B, S, H]");
+    d1 = dx1->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(ids.device());
+  const int smem = (4 + T) * H * 4;
+  vpl_dispatch(H, [&](auto v) {
+    auto k = bert_embed_bwd_kernel<decltype(v)::value>;
+    if (smem > 48 * 1024) REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    k<<<S, kWarps * 32, smem, cur_stream()>>>(
+        ids.data_ptr<int64_t>(), tt.data_ptr<int64_t>(), word.data_ptr<float>(), pos.data_ptr<float>(),
+        type.data_ptr<float>(), gamma.data_ptr<float>(), static_cast<float>(eps), B, S, static_cast<int>(word.size(0)),
+        T, dx2.data_ptr<float>(), d1, dword.data_ptr<float>(), dpos.data_ptr<float>(), dtype.data_ptr<float>(),
+        dgamma.data_ptr<float>(), dbeta.data_ptr<float>());
+  });
+  REVPP_CHECK_LAUNCH();
+}
+
+void im2col_patches(const torch::Tensor& img, int64_t patch, torch::Tensor out) {
+  check_cuda_f32(img, "img");
+  check_cuda_bf16(out, "out");
+  REVPP_CHECK(img.is_contiguous() && img.dim() == 4 && img.size(2) == img.size(3), "img [B, C, I, I]");
+  const int B = static_cast<int>(img.size(0)), C = static_cast<int>(img.size(1)), I = static_cast<int>(img.size(2));
+  const int p = static_cast<int>(patch);
+  REVPP_CHECK(I % p == 0, "image size must be a multiple of the patch size");
+  const long long n = static_cast<long long>(B) * (I / p) * (I / p) * C * p * p;
+  REVPP_CHECK(out.numel() >= n, "patch buffer too small");
+  c10::cuda::CUDAGuard guard(img.device());
+  im2col_patches_kernel<<<grid1d(n, 256), 256, 0, cur_stream()>>>(img.data_ptr<float>(),
+                                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B,
+                                                                    C, I, p);
+  REVPP_CHECK_LAUNCH();
+}
+
+void vit_assemble_fwd(const torch::Tensor& conv, const torch::Tensor& cls, const torch::Tensor& pos,
+                      const torch::Tensor& gamma, const torch::Tensor& beta, double eps, int64_t B, int64_t S,
+                      torch::Tensor out) {
+  check_cuda_bf16(conv, "conv");
+  const int H = static_cast<int>(gamma.numel());
+  c10::cuda::CUDAGuard guard(conv.device());
+  const int M = static_cast<int>(B * S);
+  vpl_dispatch(H, [&](auto v) {
+    vit_assemble_fwd_kernel<decltype(v)::value><<<(M + kWarps - 1) / kWarps, kWarps * 32, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(conv.data_ptr()), cls.data_ptr<float>(), pos.data_ptr<float>(),
+        gamma.data_ptr<float>(), beta.data_ptr<float>(), static_cast<float>(eps), static_cast<int>(B),
+        static_cast<int>(S), out.data_ptr<float>());
+  });
+  REVPP_CHECK_LAUNCH();
+}
+
+void vit_assemble_bwd(const torch::Tensor& conv, const torch::Tensor& cls, const torch::Tensor& pos,
+                      const torch::Tensor& gamma, double eps, int64_t B, int64_t S, const torch::Tensor& dx2,
+                      const c10::optional<torch::Tensor>& dx1, torch::Tensor dconv, torch::Tensor dcls,
+                      torch::Tensor dpos, torch::Tensor dgamma, torch::Tensor dbeta) {
+  const int H = static_cast<int>(gamma.numel());
+  c10::cuda::CUDAGuard guard(conv.device());
+  const float* d1 = (dx1.has_value() && dx1->defined()) ? dx1->data_ptr<float>() : nullptr;
+  const int smem = 3 * H * 4;
+  vpl_dispatch(H, [&](auto v) {
+    auto k = vit_assemble_bwd_kernel<decltype(v)::value>;
+    k<<<static_cast<unsigned>(S), kWarps * 32, smem, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(conv.data_ptr()), cls.data_ptr<float>(), pos.data_ptr<float>(),
+        gamma.data_ptr<float>(), static_cast<float>(eps), static_cast<int>(B), static_cast<int>(S),
+        dx2.data_ptr<float>(), d1, reinterpret_cast<__nv_bfloat16*>(dconv.data_ptr()), dcls.data_ptr<float>(),
+        dpos.data_ptr<float>(), dgamma.data_ptr<float>(), dbeta.data_ptr<float>());
+  });
+  REVPP_CHECK_LAUNCH();
+}
+
+// mode: 0 mean-pool of y2 + y1, 1 CLS row of y2 + y1, 2 CLS row of concat [y1, y2].
+// Returns nothing; fills logits [B, C], loss [B]; with want_grad also the parameter
+// gradients and dy2 / dy1 ([B, S, H]).
+void head_fwd_bwd(const torch::Tensor& y2, const c10::optional<torch::Tensor>& y1, int64_t mode,
+                  const torch::Tensor& gamma, const torch::Tensor& beta, double eps, const torch::Tensor& wb,
+                  const torch::Tensor& bb, const c10::optional<torch::Tensor>& labels, double grad_scale,
+                  torch::Tensor pooled, torch::Tensor logits, torch::Tensor loss, bool want_grad,
+                  const c10::optional<torch::Tensor>& dlogits, const c10::optional<torch::Tensor>& hb,
+                  const c10::optional<torch::Tensor>& dpooled, const c10::optional<torch::Tensor>& dW,
+                  const c10::optional<torch::Tensor>& db, const c10::optional<torch::Tensor>& dgamma,
+                  const c10::optional<torch::Tensor>& dbeta, const c10::optional<torch::Tensor>& dy2,
+                  const c10::optional<torch::Tensor>& dy1) {
+  check_cuda_f32(y2, "y2");
+  const int B = static_cast<int>(y2.size(0)), S = static_cast<int>(y2.size(1)), H = static_cast<int>(y2.size(2));
+  const int W = mode == 2 ? 2 * H : H;
+  const int C = static_cast<int>(wb.size(0));
+  REVPP_CHECK(wb.size(1) == W && gamma.numel() == W, "head width mismatch");
+  const float* y1p = (y1.has_value() && y1->defined()) ? y1->data_ptr<float>() : nullptr;
+  REVPP_CHECK(mode != 2 || y1p != nullptr, "concat pooling needs both streams");
+  c10::cuda::CUDAGuard guard(y2.device());
+  cudaStream_t st = cur_stream();
+  {
+    dim3 grid((W + 255) / 256, B);
+    head_pool_kernel<<<grid, 256, 0, st>>>(y2.data_ptr<float>(), y1p, B, S, H, static_cast<int>(mode),
+                                            pooled.data_ptr<float>());
+    REVPP_CHECK_LAUNCH();
+  }
+  const int threads = 256;
+  const int smem = (2 * W + C + 64) * 4;
+  auto k = head_fwd_bwd_kernel;
+  if (smem > 48 * 1024) REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t* lab = (labels.has_value() && labels->defined()) ? labels->data_ptr<int64_t>() : nullptr;
+  k<<<B, threads, smem, st>>>(
+      pooled.data_ptr<float>(), W, gamma.data_ptr<float>(), beta.data_ptr<float>(), static_cast<float>(eps),
+      reinterpret_cast<const __nv_bfloat16*>(wb.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(bb.data_ptr()), C,
+      lab, static_cast<float>(grad_scale), B, logits.data_ptr<float>(), loss.data_ptr<float>(),
+      want_grad ? dlogits->data_ptr<float>() : nullptr,
+      want_grad ? reinterpret_cast<__nv_bfloat16*>(hb->data_ptr()) : nullptr,
+      want_grad ? dpooled->data_ptr<float>() : nullptr, want_grad ? dgamma->data_ptr<float>() : nullptr,
+      want_grad ? dbeta->data_ptr<float>() : nullptr, want_grad ? 1 : 0, status_device_ptr());
+  REVPP_CHECK_LAUNCH();
+  if (!want_grad) return;
+  {
+    const long long n = static_cast<long long>(C) * W;
+    head_wgrad_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+        dlogits->data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(hb->data_ptr()), B, C, W,
+        dW->data_ptr<float>(), db->data_ptr<float>());
+    REVPP_CHECK_LAUNCH();
+  }
+  {
+    const long long n4 = static_cast<long long>(B) * S * H / 4;
+    float* d1p = (dy1.has_value() && dy1->defined()) ? dy1->data_ptr<float>() : nullptr;
+    head_spread_kernel<<<grid1d(n4, 256), 256, 0, st>>>(dpooled->data_ptr<float>(), B, S, H, static_cast<int>(mode),
+                                                        dy2->data_ptr<float>(), d1p);
+    REVPP_CHECK_LAUNCH();
+  }
+}
+
+}  // namespace revpp

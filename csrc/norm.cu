@@ -159,33 +159,47 @@ __global__ void __launch_bounds__(kLnWarps * 32)
 
 // out_bf16 = bf16(in_f32) and colsum += sum_rows(in), in fp32 [M, N].
 // Or, with a bf16 input, only the column sum.
+// Tile = 128 rows x 256 columns per CTA: 64 threads x 4 columns across, 4 row groups
+// down; the row groups are reduced in shared memory, so each column sees one atomic per
+// 128 rows.
+constexpr int kColTileRows = 128;
 template <bool IN_BF16>
 __global__ void __launch_bounds__(256)
     cast_colsum_kernel(const void* __restrict__ in_, long long ldi, int M, int N, __nv_bfloat16* __restrict__ out,
-                       long long ldo, float* __restrict__ colsum, int rows_per_block) {
-  // Each thread owns 4 consecutive columns; blockDim.x * 4 columns per block column-slab.
-  const int c4 = blockIdx.y * blockDim.x + threadIdx.x;
-  if (4 * c4 >= N) return;
-  const int r0 = blockIdx.x * rows_per_block;
-  const int r1 = min(M, r0 + rows_per_block);
+                       long long ldo, float* __restrict__ colsum) {
+  __shared__ float4 red[3][64];
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const int c4 = blockIdx.y * 64 + tx;
+  const bool col_ok = 4 * c4 < N;
+  const int r0 = blockIdx.x * kColTileRows;
+  const int r1 = min(M, r0 + kColTileRows);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int r = r0; r < r1; ++r) {
-    float4 v;
-    if constexpr (IN_BF16) {
-      const uint2 p = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(in_) +
-                                                      static_cast<long long>(r) * ldi + 4 * c4);
-      const float2 a = unpack_bf16x2(p.x), b = unpack_bf16x2(p.y);
-      v = make_float4(a.x, a.y, b.x, b.y);
-    } else {
-      v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in_) + static_cast<long long>(r) * ldi + 4 * c4);
-      if (out) {
-        *reinterpret_cast<uint2*>(out + static_cast<long long>(r) * ldo + 4 * c4) =
-            make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  if (col_ok) {
+    for (int r = r0 + ty; r < r1; r += 4) {
+      float4 v;
+      if constexpr (IN_BF16) {
+        const uint2 p = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(in_) +
+                                                        static_cast<long long>(r) * ldi + 4 * c4);
+        const float2 a = unpack_bf16x2(p.x), b = unpack_bf16x2(p.y);
+        v = make_float4(a.x, a.y, b.x, b.y);
+      } else {
+        v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in_) + static_cast<long long>(r) * ldi +
+                                             4 * c4);
+        if (out) {
+          *reinterpret_cast<uint2*>(out + static_cast<long long>(r) * ldo + 4 * c4) =
+              make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        }
       }
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
-    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
   }
-  if (colsum) {
+  if (ty > 0) red[ty - 1][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && col_ok && colsum) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      acc.x += red[k][tx].x; acc.y += red[k][tx].y; acc.z += red[k][tx].z; acc.w += red[k][tx].w;
+    }
     atomicAdd(colsum + 4 * c4 + 0, acc.x);
     atomicAdd(colsum + 4 * c4 + 1, acc.y);
     atomicAdd(colsum + 4 * c4 + 2, acc.z);
@@ -294,7 +308,7 @@ void layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch:
 // fp32 in: out = bf16(in) (optional) and colsum += column sums (optional).  bf16 in: colsum only.
 void cast_colsum(const torch::Tensor& in, const c10::optional<torch::Tensor>& out,
                  const c10::optional<torch::Tensor>& colsum) {
-  REVPP_CHECK(in.is_cuda() && in.dim() == 2 && in.stride(1) == 1);
+  REVPP_CHECK(in.is_cuda() && in.dim() == 2 && in.stride(1) == 1, "input must be a 2-D CUDA tensor, unit inner stride");
   const int M = static_cast<int>(in.size(0)), N = static_cast<int>(in.size(1));
   REVPP_CHECK(N % 4 == 0, "cast_colsum needs N % 4 == 0");
   if (M == 0) return;
@@ -307,21 +321,12 @@ void cast_colsum(const torch::Tensor& in, const c10::optional<torch::Tensor>& ou
     ldo = out->stride(0);
   }
   float* cs = opt_f32(colsum);
-  const int threads = 256;
-  const int col_blocks = (N / 4 + threads - 1) / threads;
-  // Aim for ~4 waves of blocks over the machine.
-  int row_blocks = std::max(1, (4 * num_sms()) / col_blocks);
-  int rows_per_block = (M + row_blocks - 1) / row_blocks;
-  rows_per_block = std::max(rows_per_block, 16);
-  row_blocks = (M + rows_per_block - 1) / rows_per_block;
-  dim3 grid(row_blocks, col_blocks);
+  dim3 grid((M + kColTileRows - 1) / kColTileRows, (N / 4 + 63) / 64);
   if (in.scalar_type() == at::kBFloat16) {
-    cast_colsum_kernel<true><<<grid, threads, 0, cur_stream()>>>(in.data_ptr(), in.stride(0), M, N, nullptr, 0, cs,
-                                                                  rows_per_block);
+    cast_colsum_kernel<true><<<grid, 256, 0, cur_stream()>>>(in.data_ptr(), in.stride(0), M, N, nullptr, 0, cs);
   } else {
     check_cuda_f32(in, "in");
-    cast_colsum_kernel<false><<<grid, threads, 0, cur_stream()>>>(in.data_ptr(), in.stride(0), M, N, op, ldo, cs,
-                                                                   rows_per_block);
+    cast_colsum_kernel<false><<<grid, 256, 0, cur_stream()>>>(in.data_ptr(), in.stride(0), M, N, op, ldo, cs);
   }
   REVPP_CHECK_LAUNCH();
 }

@@ -216,20 +216,27 @@ class KernelMath:
         return out, ctx
 
     # -------------------------------------------------------------- VJPs
-    def g_vjp(self, blk: EncoderBlock, ctx, dy, resid_grad, out: Optional[torch.Tensor] = None):
-        """dx = resid_grad + dG/dx^T dy  for G(x) = W2 gelu(W1 LN2(x) + b1) + b2."""
+    def g_vjp(self, blk: EncoderBlock, ctx, dy, resid_grad, out: Optional[torch.Tensor] = None,
+              dy_bf16: Optional[torch.Tensor] = None, out_colsum: Optional[torch.Tensor] = None):
+        """dx = resid_grad + dG/dx^T dy  for G(x) = W2 gelu(W1 LN2(x) + b1) + b2.
+
+        ``dy_bf16``: bf16 copy of dy whose column sums are already in this block's b2
+        gradient (fused into the previous LayerNorm backward).  ``out_colsum``: where the
+        LayerNorm backward also accumulates the column sums of dx (the out-proj bias
+        gradient when dx feeds F's VJP)."""
         ops = self.ops
         w = self.views(blk)
         B, S, H = dy.shape
         M = B * S
         I = w.w1.shape[0]
         dy2d = dy.view(M, H)
-        dyb = self.scratch("g_dyb", (M, H), torch.bfloat16)
         du = self.scratch("g_du", (M, I), torch.bfloat16)
         dln = self.scratch("g_dln", (M, H), torch.bfloat16)
-        ops.cast_colsum(dy2d, out=dyb, colsum=w.d_b2)                   # bf16(dy), db2 += sum(dy)
-        ops.linear_wgrad(dyb, ctx.h, w.d_w2)                            # dW2 += dy^T h
-        ops.linear_dgrad(dyb, w.w2, du, epi=ops.EPI_DGELU, aux=ctx.u)   # du = (dy W2) * gelu'(u)
+        if dy_bf16 is None:
+            dy_bf16 = self.scratch("g_dyb", (M, H), torch.bfloat16)
+            ops.cast_colsum(dy2d, out=dy_bf16, colsum=w.d_b2)           # bf16(dy), db2 += sum(dy)
+        ops.linear_wgrad(dy_bf16, ctx.h, w.d_w2)                        # dW2 += dy^T h
+        ops.linear_dgrad(dy_bf16, w.w2, du, epi=ops.EPI_DGELU, aux=ctx.u)  # du = (dy W2) * gelu'(u)
         ops.cast_colsum(du, colsum=w.d_b1)                              # db1 += sum(du)
         ops.linear_wgrad(du, ctx.b, w.d_w1)                             # dW1 += du^T LN2(x)
         ops.linear_dgrad(du, w.w1, dln)                                 # d LN2 out = du W1
@@ -238,13 +245,18 @@ class KernelMath:
         dxb = self.scratch("g_dxb", (M, H), torch.bfloat16)
         ops.layernorm_bwd(dln, ctx.x.view(M, H), w.ln2_w, ctx.mean, ctx.rstd, dgamma=w.d_ln2_w, dbeta=w.d_ln2_b,
                           resid=None if resid_grad is None else resid_grad.view(M, H), dx_f32=out.view(M, H),
-                          dx_bf16=dxb)
+                          dx_bf16=dxb, colsum=out_colsum)
         ctx.dx_bf16 = dxb
+        ctx.dx_colsum_done = out_colsum is not None
         return out
 
     def f_vjp(self, blk: EncoderBlock, ctx, dy, resid_grad, out: Optional[torch.Tensor] = None,
-              dy_bf16: Optional[torch.Tensor] = None):
-        """dx = resid_grad + dF/dx^T dy  for F(x) = Wo attn(Wqkv LN1(x) + bqkv) + bo."""
+              dy_bf16: Optional[torch.Tensor] = None, colsum_done: bool = False,
+              out_bf16: Optional[torch.Tensor] = None, out_colsum: Optional[torch.Tensor] = None):
+        """dx = resid_grad + dF/dx^T dy  for F(x) = Wo attn(Wqkv LN1(x) + bqkv) + bo.
+
+        ``out_bf16`` / ``out_colsum``: the LayerNorm backward also writes bf16(dx) and adds
+        the column sums of dx there (the next G VJP's operand and bias gradient)."""
         ops = self.ops
         w = self.views(blk)
         B, S, H = dy.shape
@@ -253,7 +265,7 @@ class KernelMath:
         if dy_bf16 is None:
             dy_bf16 = self.scratch("f_dyb", (M, H), torch.bfloat16)
             ops.cast_colsum(dy2d, out=dy_bf16, colsum=w.d_bo)
-        else:
+        elif not colsum_done:
             ops.cast_colsum(dy2d, colsum=w.d_bo)
         do = self.scratch("f_do", (M, H), torch.bfloat16)
         dqkv = self.scratch("f_dqkv", (M, 3 * H), torch.bfloat16)
@@ -269,7 +281,8 @@ class KernelMath:
         if out is None:
             out = torch.empty_like(dy)
         ops.layernorm_bwd(dln, ctx.x.view(M, H), w.ln1_w, ctx.mean, ctx.rstd, dgamma=w.d_ln1_w, dbeta=w.d_ln1_b,
-                          resid=None if resid_grad is None else resid_grad.view(M, H), dx_f32=out.view(M, H))
+                          resid=None if resid_grad is None else resid_grad.view(M, H), dx_f32=out.view(M, H),
+                          dx_bf16=out_bf16, colsum=out_colsum)
         return out
 
 
@@ -296,15 +309,28 @@ def rev_block_recover(math_, blk: EncoderBlock, y2, y1):
     return SimpleNamespace(x2=x2, x1=x1, ctx_g=ctx_g, ctx_f=ctx_f)
 
 
-def rev_block_grads(math_, blk: EncoderBlock, rc, dy2, dy1):
+def rev_block_grads(math_, blk: EncoderBlock, rc, dy2, dy1, dy2_bf16=None, prev_blk: Optional[EncoderBlock] = None):
     """dY1' = dY1 + dG/dY1^T dY2;  dX2 = dY2 + dF/dX2^T dY1';  dX1 = dY1'
-    (BERT/models/reversible.py:90-110).  Returns (dX2, dX1)."""
-    dy1p = math_.g_vjp(blk, rc.ctx_g, dy2, dy1)
+    (BERT/models/reversible.py:90-110).  Returns (dX2, dX1, bf16(dX2) or None).
+
+    Kernel path fusions: the LayerNorm backward of G also sums dY1' into the out-proj bias
+    gradient and writes its bf16 copy for F's VJP; with ``prev_blk`` the LayerNorm backward
+    of F writes bf16(dX2) and sums it into the previous block's FFN2 bias gradient, which
+    is exactly what that block's G VJP needs first."""
     if isinstance(math_, KernelMath):
-        dx2 = math_.f_vjp(blk, rc.ctx_f, dy1p, dy2, dy_bf16=rc.ctx_g.dx_bf16)
-    else:
-        dx2 = math_.f_vjp(blk, rc.ctx_f, dy1p, dy2)
-    return dx2, dy1p
+        w = math_.views(blk)
+        dy1p = math_.g_vjp(blk, rc.ctx_g, dy2, dy1, dy_bf16=dy2_bf16, out_colsum=w.d_bo)
+        nxt_bf16 = nxt_colsum = None
+        if prev_blk is not None:
+            B, S, H = dy2.shape
+            nxt_bf16 = torch.empty(B * S, H, dtype=torch.bfloat16, device=dy2.device)
+            nxt_colsum = math_.views(prev_blk).d_b2
+        dx2 = math_.f_vjp(blk, rc.ctx_f, dy1p, dy2, dy_bf16=rc.ctx_g.dx_bf16, colsum_done=True,
+                          out_bf16=nxt_bf16, out_colsum=nxt_colsum)
+        return dx2, dy1p, nxt_bf16
+    dy1p = math_.g_vjp(blk, rc.ctx_g, dy2, dy1)
+    dx2 = math_.f_vjp(blk, rc.ctx_f, dy1p, dy2)
+    return dx2, dy1p, None
 
 
 def std_block_forward(math_, blk: EncoderBlock, x, save: bool):
@@ -316,9 +342,10 @@ def std_block_forward(math_, blk: EncoderBlock, x, save: bool):
 
 def std_block_backward(math_, blk: EncoderBlock, ctxs, dx2):
     cf, cg = ctxs
-    dx1 = math_.g_vjp(blk, cg, dx2, dx2)
     if isinstance(math_, KernelMath):
-        return math_.f_vjp(blk, cf, dx1, dx1, dy_bf16=cg.dx_bf16)
+        dx1 = math_.g_vjp(blk, cg, dx2, dx2, out_colsum=math_.views(blk).d_bo)
+        return math_.f_vjp(blk, cf, dx1, dx1, dy_bf16=cg.dx_bf16, colsum_done=True)
+    dx1 = math_.g_vjp(blk, cg, dx2, dx2)
     return math_.f_vjp(blk, cf, dx1, dx1)
 
 

@@ -124,7 +124,9 @@ class TorchEmbedHead:
         with torch.no_grad():
             return self._embed(inputs).contiguous()
 
-    def embed_bwd(self, inputs, dx: torch.Tensor) -> None:
+    def embed_bwd(self, inputs, dx: torch.Tensor, dx1: Optional[torch.Tensor] = None) -> None:
+        if dx1 is not None:
+            dx = dx + dx1  # the coupling duplicated the embedding into both streams
         params = list(self.stage.embeddings.parameters())
         with torch.enable_grad():
             x = self._embed(inputs)

@@ -60,10 +60,13 @@ def rev_backward(math_, blocks: Sequence[EncoderBlock], y2, y1, dy2, dy1, parepr
         if not pareprop or streams is None or not y2.is_cuda:
             rc = rev_block_recover(math_, blocks[-1], y2, y1)
             dy = (dy2, dy1)
+            dyb = None
             for i in range(n - 1, -1, -1):
                 if on_recover is not None:
                     on_recover(i, rc.x2, rc.x1)
-                dy = rev_block_grads(math_, blocks[i], rc, *dy)
+                prev = blocks[i - 1] if i > 0 else None
+                dx2, dx1, dyb = rev_block_grads(math_, blocks[i], rc, dy[0], dy[1], dy2_bf16=dyb, prev_blk=prev)
+                dy = (dx2, dx1)
                 if i > 0:
                     rc = rev_block_recover(math_, blocks[i - 1], rc.x2, rc.x1)
             return dy, (rc.x2, rc.x1)
@@ -85,6 +88,7 @@ def _pareprop_backward(math_, blocks, y2, y1, dy2, dy1, streams, on_recover):
         rc = rev_block_recover(math_, blocks[n - 1], y2, y1)
         f_ev[0].record(s1)
     dy = (dy2, dy1)
+    dyb = None
     # step i handles block n-1-i: gradient on one stream, reconstruction of the next on the other
     for i in range(n - 1):
         this_blk = blocks[n - 1 - i]
@@ -92,14 +96,15 @@ def _pareprop_backward(math_, blocks, y2, y1, dy2, dy1, streams, on_recover):
         s_grad, s_rec = (s1, s2) if i % 2 == 0 else (s2, s1)
         _record_ctx(rc, s_grad)
         _record_ctx(rc, s_rec)
-        _record(list(dy), s_grad)
+        _record(list(dy) + [dyb], s_grad)
         with torch.cuda.stream(s_grad):
             if i > 0:
                 s_grad.wait_event(b_ev[i - 1])
             s_grad.wait_event(f_ev[i])
             if on_recover is not None:
                 on_recover(n - 1 - i, rc.x2, rc.x1)
-            dy = rev_block_grads(math_, this_blk, rc, *dy)
+            dx2, dx1, dyb = rev_block_grads(math_, this_blk, rc, dy[0], dy[1], dy2_bf16=dyb, prev_blk=next_blk)
+            dy = (dx2, dx1)
             b_ev[i].record(s_grad)
         with torch.cuda.stream(s_rec):
             s_rec.wait_event(f_ev[i])
@@ -107,14 +112,15 @@ def _pareprop_backward(math_, blocks, y2, y1, dy2, dy1, streams, on_recover):
             f_ev[i + 1].record(s_rec)
     s_grad = s1 if (n - 1) % 2 == 0 else s2
     _record_ctx(rc, s_grad)
-    _record(list(dy), s_grad)
+    _record(list(dy) + [dyb], s_grad)
     with torch.cuda.stream(s_grad):
         if n > 1:
             s_grad.wait_event(b_ev[n - 2])
         s_grad.wait_event(f_ev[n - 1])
         if on_recover is not None:
             on_recover(0, rc.x2, rc.x1)
-        dy = rev_block_grads(math_, blocks[0], rc, *dy)
+        dx2, dx1, _ = rev_block_grads(math_, blocks[0], rc, dy[0], dy[1], dy2_bf16=dyb)
+        dy = (dx2, dx1)
         b_ev[n - 1].record(s_grad)
     main.wait_stream(s1)
     main.wait_stream(s2)

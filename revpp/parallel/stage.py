@@ -150,7 +150,7 @@ class ReversibleStage(StageBase):
             self._record_actv_err(mb, (x2, x1), self.fwd_input_copy.pop(mb))
         if self.is_first:
             inputs = self.input_cache.pop(mb)
-            self.eh.embed_bwd(inputs, dx2 + dx1)
+            self.eh.embed_bwd(inputs, dx2, dx1)
             return None
         return (dx2, dx1, x2, x1)
 
@@ -279,9 +279,15 @@ class InverseStage(StageBase):
         return (y2, y1)
 
     def backward(self, mb, msg):
+        inputs = None
         if self.is_last:
             y2, y1, dy2, dy1 = self.last_cache.pop(mb)
-            x2, x1 = inverse_sequence(self.math, self.blocks, y2, y1)
+            if self.is_first:  # single stage: recompute from the cached inputs
+                inputs = self.input_cache.pop(mb)
+                x = self.eh.embed_fwd(inputs)
+                x2, x1 = x, x
+            else:
+                x2, x1 = inverse_sequence(self.math, self.blocks, y2, y1)
         elif self.is_first:
             dy2, dy1 = msg[0], msg[1]
             inputs = self.input_cache.pop(mb)
@@ -303,10 +309,11 @@ class InverseStage(StageBase):
                 a2, a1 = y2_, y1_
             dy = (dy2, dy1)
             for blk, rc in zip(reversed(self.blocks), reversed(rcs)):
-                dy = rev_block_grads(self.math, blk, rc, *dy)
+                dx2_, dx1_, _ = rev_block_grads(self.math, blk, rc, *dy)
+                dy = (dx2_, dx1_)
         dx2, dx1 = dy
         if self.is_first:
-            self.eh.embed_bwd(inputs, dx2 + dx1)
+            self.eh.embed_bwd(inputs, dx2, dx1)
             return None
         if self.stage_index == 1:
             return (dx2, dx1)
