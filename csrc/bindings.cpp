@@ -1,6 +1,8 @@
 // Python bindings of the revpp CUDA extension (module revpp._C).
 #include <torch/extension.h>
 
+#include <vector>
+
 #include "host.h"
 
 namespace revpp {
@@ -33,6 +35,16 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
                 double wd, int64_t step, double max_norm, const c10::optional<torch::Tensor>& sumsq,
                 bool zero_grad);
 void scale_(torch::Tensor x, double s);
+// attention_tc.cu
+void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
+                 int64_t heads);
+// comm.cu
+void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
+                     const std::vector<int64_t>& shadow_ptrs, const std::vector<int64_t>& flag_ptrs, torch::Tensor m,
+                     torch::Tensor v, torch::Tensor scratch, int64_t n, int64_t rank, int64_t epoch, double lr,
+                     double beta1, double beta2, double eps, double wd, int64_t step, double max_norm,
+                     double timeout_s, bool zero_grad);
+void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch::Tensor result);
 // embed_head.cu
 void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
                     const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
@@ -92,6 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dx_f32") = py::none(), py::arg("dx_bf16") = py::none(), py::arg("colsum") = py::none());
   m.def("attn_fwd", &revpp::attn_fwd, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"),
         py::arg("heads"));
+  m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
+        py::arg("S"), py::arg("heads"));
   m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
         py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("bert_embed_fwd", &revpp::bert_embed_fwd);
@@ -109,6 +123,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("hb") = py::none(), py::arg("dpooled") = py::none(), py::arg("dW") = py::none(),
         py::arg("db") = py::none(), py::arg("dgamma") = py::none(), py::arg("dbeta") = py::none(),
         py::arg("dy2") = py::none(), py::arg("dy1") = py::none());
+  m.def("dp_reduce_adamw", &revpp::dp_reduce_adamw);
+  m.def("flag_wait_probe", &revpp::flag_wait_probe, py::arg("flag"), py::arg("expect"), py::arg("timeout_s"),
+        py::arg("result"));
   m.def("cast_colsum", &revpp::cast_colsum, py::arg("inp"), py::arg("out") = py::none(),
         py::arg("colsum") = py::none());
 }

@@ -1,0 +1,259 @@
+// Cross-GPU kernels over NVLink peer memory, and the bounded-wait primitives they use.
+//
+// dp_reduce_adamw: gradient all-reduce across D pipeline replicas fused with the gradient
+// average, the clip-norm and the AdamW update, in one cooperative kernel per GPU.  Every
+// rank maps its peers' flat buffers (CUDA IPC) and
+//   0. flag barrier: every replica's backward has finished writing its gradients;
+//   A. reduces its own shard r: g = (sum_d grad_d[shard r]) / D, read from the peers with
+//      plain loads over NVLink, written back into its own grad[shard r]; squared-norm
+//      partials accumulate on the way;
+//   B. publishes its partial squared norm into every peer's flag page and raises its epoch
+//      flag there (system-scope fence first); waits, with a time limit, until every peer's
+//      flag in its own page shows this epoch, and sums the norms: clip coefficient;
+//   C. applies AdamW to shard r (own m / v) and stores the new fp32 parameters and the bf16
+//      shadow into its own buffers *and every peer's*; zeroes its whole gradient buffer
+//      (the peers finished reading it before step B's barrier);
+//   D. second flag barrier: no rank leaves until every peer's parameter stores are visible.
+// Traffic per rank: (D-1)/D of the gradient in, (D-1)/D of the parameters (fp32 + bf16)
+// out, no intermediate copies.  No TMA is used here, so no multicast load can touch peer
+// memory.  Every wait gives up after `timeout_ns`, records kStatusFlagTimeout and returns.
+//
+// flag_wait_probe: a one-thread kernel that waits on a flag nobody sets, used by tests to
+// check that the bounded wait reports an error instead of hanging.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "host.h"
+
+namespace cg = cooperative_groups;
+
+namespace revpp {
+
+constexpr int kMaxPeers = 8;
+// flag page layout (int32 words): [0, 64) epoch flags per rank, [64, 128) norm bits per rank
+constexpr int kFlagEpoch = 0;
+constexpr int kFlagNorm = 64;
+constexpr int kFlagWords = 128;
+
+struct DpArgs {
+  float* grad[kMaxPeers];
+  float* param[kMaxPeers];
+  __nv_bfloat16* shadow[kMaxPeers];
+  int* flags[kMaxPeers];
+  float* m;
+  float* v;
+  float* sumsq_scratch;  // own, 2 floats
+  long long n;           // elements in the flat buffers (multiple of 4 * D)
+  int D, rank, epoch, zero_grad;
+  float lr, beta1, beta2, eps, wd, step_size, inv_bc2_sqrt, max_norm, inv_d;
+  long long timeout_ns;
+  int* status;
+};
+
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
+
+// Wait until flags[idx(d)] >= epoch for every rank d (in our own page).  Returns false on timeout.
+__device__ bool wait_all_flags(int* own_flags, int D, int epoch, long long timeout_ns, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int d = 0; d < D; ++d) {
+    while (ld_volatile(own_flags + kFlagEpoch + d) < epoch) {
+      if (globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
+        atomicOr(status, kStatusFlagTimeout);
+        return false;
+      }
+      __nanosleep(256);
+    }
+  }
+  __threadfence_system();
+  return true;
+}
+
+__global__ void __launch_bounds__(512) dp_reduce_adamw_kernel(DpArgs a) {
+  cg::grid_group grid = cg::this_grid();
+  __shared__ float red[32];
+  __shared__ float s_coef;
+  __shared__ int s_ok;
+  const long long shard = a.n / a.D;
+  const long long lo4 = (a.rank * shard) / 4, hi4 = ((a.rank + 1) * shard) / 4;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long nthreads = static_cast<long long>(gridDim.x) * blockDim.x;
+  const int base = 3 * a.epoch;
+  // ---- barrier 0: every replica's backward has finished writing its gradients
+  if (tid == 0) {
+    a.sumsq_scratch[0] = 0.f;
+    __threadfence_system();
+    for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 1);
+    a.sumsq_scratch[1] = wait_all_flags(a.flags[a.rank], a.D, base + 1, a.timeout_ns, a.status) ? 1.f : -1.f;
+  }
+  grid.sync();
+  if (reinterpret_cast<volatile float*>(a.sumsq_scratch)[1] < 0.f) return;
+
+  // ---- A: reduce my shard, norm partials
+  float acc = 0.f;
+  for (long long i = lo4 + tid; i < hi4; i += nthreads) {
+    float4 s = reinterpret_cast<const float4*>(a.grad[a.rank])[i];
+    for (int d = 0; d < a.D; ++d) {
+      if (d == a.rank) continue;
+      const float4 g = reinterpret_cast<const float4*>(a.grad[d])[i];
+      s.x += g.x; s.y += g.y; s.z += g.z; s.w += g.w;
+    }
+    s.x *= a.inv_d; s.y *= a.inv_d; s.z *= a.inv_d; s.w *= a.inv_d;
+    reinterpret_cast<float4*>(a.grad[a.rank])[i] = s;
+    acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) atomicAdd(a.sumsq_scratch, v);
+  }
+  grid.sync();
+
+  // ---- B: exchange norms, barrier 1
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const float mine = a.sumsq_scratch[0];
+    for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagNorm + a.rank, __float_as_int(mine));
+    __threadfence_system();
+    for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 2);
+    int ok = wait_all_flags(a.flags[a.rank], a.D, base + 2, a.timeout_ns, a.status) ? 1 : 0;
+    float total = 0.f;
+    for (int d = 0; d < a.D; ++d) total += __int_as_float(ld_volatile(a.flags[a.rank] + kFlagNorm + d));
+    float coef = 1.f;
+    if (a.max_norm > 0.f) coef = fminf(1.f, a.max_norm / (sqrtf(total) + 1e-6f));
+    a.sumsq_scratch[1] = ok ? coef : -1.f;
+  }
+  grid.sync();
+  if (threadIdx.x == 0) {
+    const float c = reinterpret_cast<volatile float*>(a.sumsq_scratch)[1];
+    s_coef = c;
+    s_ok = c >= 0.f;
+  }
+  __syncthreads();
+  if (!s_ok) return;  // a peer never arrived: leave parameters untouched, error is recorded
+  const float coef = s_coef;
+
+  // ---- C: AdamW on my shard, broadcast parameters to every replica
+  const float decay = 1.f - a.lr * a.wd;
+  for (long long i = lo4 + tid; i < hi4; i += nthreads) {
+    const float4 gg = reinterpret_cast<const float4*>(a.grad[a.rank])[i];
+    if (a.zero_grad) reinterpret_cast<float4*>(a.grad[a.rank])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 p = reinterpret_cast<float4*>(a.param[a.rank])[i];
+    float4 m = reinterpret_cast<float4*>(a.m)[i];
+    float4 v = reinterpret_cast<float4*>(a.v)[i];
+    const float g4[4] = {gg.x * coef, gg.y * coef, gg.z * coef, gg.w * coef};
+    float* pp = &p.x;
+    float* mp = &m.x;
+    float* vp = &v.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mp[j] = a.beta1 * mp[j] + (1.f - a.beta1) * g4[j];
+      vp[j] = a.beta2 * vp[j] + (1.f - a.beta2) * g4[j] * g4[j];
+      pp[j] = pp[j] * decay - a.step_size * mp[j] / (sqrtf(vp[j]) * a.inv_bc2_sqrt + a.eps);
+    }
+    reinterpret_cast<float4*>(a.m)[i] = m;
+    reinterpret_cast<float4*>(a.v)[i] = v;
+    const uint2 sh = make_uint2(pack_bf16x2(p.x, p.y), pack_bf16x2(p.z, p.w));
+    for (int d = 0; d < a.D; ++d) {
+      reinterpret_cast<float4*>(a.param[d])[i] = p;
+      if (a.shadow[d]) reinterpret_cast<uint2*>(a.shadow[d])[i] = sh;
+    }
+  }
+  if (a.zero_grad) {
+    // the rest of this rank's gradient buffer: the peers finished reading it before barrier 1
+    const long long n4 = a.n / 4;
+    for (long long i = tid; i < n4; i += nthreads) {
+      if (i >= lo4 && i < hi4) continue;
+      reinterpret_cast<float4*>(a.grad[a.rank])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  __threadfence_system();
+  grid.sync();
+
+  // ---- D: barrier 2 (every replica's parameter stores are visible)
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 3);
+    wait_all_flags(a.flags[a.rank], a.D, base + 3, a.timeout_ns, a.status);
+  }
+}
+
+__global__ void flag_wait_probe_kernel(int* flag, int expect, long long timeout_ns, int* status, int* result) {
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_volatile(flag) < expect) {
+    if (globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
+      atomicOr(status, kStatusFlagTimeout);
+      *result = -1;
+      return;
+    }
+    __nanosleep(1000);
+  }
+  *result = 1;
+}
+
+// ------------------------------------------------------------------ host side
+void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
+                     const std::vector<int64_t>& shadow_ptrs, const std::vector<int64_t>& flag_ptrs, torch::Tensor m,
+                     torch::Tensor v, torch::Tensor scratch, int64_t n, int64_t rank, int64_t epoch, double lr,
+                     double beta1, double beta2, double eps, double wd, int64_t step, double max_norm,
+                     double timeout_s, bool zero_grad) {
+  const int D = static_cast<int>(grad_ptrs.size());
+  REVPP_CHECK(D >= 1 && D <= kMaxPeers, "1..8 replicas");
+  REVPP_CHECK(param_ptrs.size() == static_cast<size_t>(D) && flag_ptrs.size() == static_cast<size_t>(D),
+              "one pointer per replica");
+  REVPP_CHECK(n % (4 * D) == 0, "flat size must be a multiple of 4 * replicas");
+  check_cuda_f32(m, "m");
+  check_cuda_f32(v, "v");
+  check_cuda_f32(scratch, "scratch");
+  c10::cuda::CUDAGuard guard(m.device());
+  DpArgs a{};
+  for (int d = 0; d < D; ++d) {
+    a.grad[d] = reinterpret_cast<float*>(grad_ptrs[d]);
+    a.param[d] = reinterpret_cast<float*>(param_ptrs[d]);
+    a.shadow[d] = shadow_ptrs.empty() ? nullptr : reinterpret_cast<__nv_bfloat16*>(shadow_ptrs[d]);
+    a.flags[d] = reinterpret_cast<int*>(flag_ptrs[d]);
+  }
+  a.m = m.data_ptr<float>();
+  a.v = v.data_ptr<float>();
+  a.sumsq_scratch = scratch.data_ptr<float>();
+  a.n = n;
+  a.D = D;
+  a.rank = static_cast<int>(rank);
+  a.epoch = static_cast<int>(epoch);
+  a.zero_grad = zero_grad ? 1 : 0;
+  const double bc1 = 1.0 - std::pow(beta1, static_cast<double>(step));
+  const double bc2 = 1.0 - std::pow(beta2, static_cast<double>(step));
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.wd = static_cast<float>(wd);
+  a.step_size = static_cast<float>(lr / bc1);
+  a.inv_bc2_sqrt = static_cast<float>(1.0 / std::sqrt(bc2));
+  a.max_norm = static_cast<float>(max_norm);
+  a.inv_d = 1.f / D;
+  a.timeout_ns = static_cast<long long>(timeout_s * 1e9);
+  a.status = status_device_ptr();
+  int per_sm = 0;
+  REVPP_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dp_reduce_adamw_kernel, 512, 0));
+  REVPP_CHECK(per_sm >= 1, "dp kernel cannot be resident");
+  const int grid = std::max(1, std::min(per_sm, 2) * gemm_grid_sms());
+  void* params[] = {&a};
+  REVPP_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(dp_reduce_adamw_kernel), dim3(grid), dim3(512),
+                                               params, 0, cur_stream()));
+  count_launch();
+}
+
+// Waits (one thread) until *flag >= expect or the time limit passes; result[0] = 1 or -1.
+void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch::Tensor result) {
+  REVPP_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt, "flag must be an int32 CUDA tensor");
+  REVPP_CHECK(result.is_cuda() && result.scalar_type() == at::kInt, "result must be an int32 CUDA tensor");
+  c10::cuda::CUDAGuard guard(flag.device());
+  flag_wait_probe_kernel<<<1, 1, 0, cur_stream()>>>(flag.data_ptr<int>(), static_cast<int>(expect),
+                                                    static_cast<long long>(timeout_s * 1e9), status_device_ptr(),
+                                                    result.data_ptr<int>());
+  REVPP_CHECK_LAUNCH();
+}
+
+}  // namespace revpp

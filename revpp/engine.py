@@ -96,14 +96,20 @@ class Trainer:
             # the bwd channel into this stage carries the next stage's message layout
             if self.comms.bwd_in is not None:
                 self.comms.bwd_in.specs = self.stage.bwd_specs(self.stage_index)
+            from revpp.parallel.p2p import _warm_group
+
             if self.D > 1:
                 for s in range(self.P):
-                    g = dist.new_group([d * self.P + s for d in range(self.D)])
+                    ranks = [d * self.P + s for d in range(self.D)]
+                    g = dist.new_group(ranks)
+                    _warm_group(g, ranks, self.device)
                     if s == self.stage_index:
                         self.dp_group = g
             if self.P > 1:
                 for d in range(self.D):
-                    g = dist.new_group(list(range(d * self.P, (d + 1) * self.P)))
+                    ranks = list(range(d * self.P, (d + 1) * self.P))
+                    g = dist.new_group(ranks)
+                    _warm_group(g, ranks, self.device)
                     if d == self.replica:
                         self.pp_group = g
         if self.P > 1 and self.device.type == "cuda":
@@ -119,6 +125,11 @@ class Trainer:
         if self.D > 1:
             from revpp.parallel.allreduce import make_reducer
 
+            # replicas start from the first replica's weights (DistributedDataParallel does the
+            # same broadcast when it wraps the module)
+            src = self.stage_index  # replica 0 of this stage
+            dist.broadcast(self.flat.data, src=src, group=self.dp_group)
+            self.flat.refresh_shadow()
             self.dp_reducer = make_reducer(self, cfg)
         self.step_count = 0
 

@@ -6,6 +6,7 @@ current stream; there is no PyTorch fallback on the GPU.  CPU execution goes thr
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -69,8 +70,16 @@ def cast_colsum(inp, out=None, colsum=None):
     ext().cast_colsum(inp, out=out, colsum=colsum)
 
 
+_ATTN_TC = os.environ.get("REVPP_ATTN_TC", "1") != "0"
+
+
 def attention_fwd(qkv, out, lse, B, S, heads):
-    ext().attn_fwd(qkv, out, lse, B, S, heads)
+    """Flash attention forward: the tcgen05 kernel (REVPP_ATTN_TC=0 selects the warp-level
+    mma.sync kernel, kept as the comparison point)."""
+    if _ATTN_TC:
+        ext().attn_fwd_tc(qkv, out, lse, B, S, heads)
+    else:
+        ext().attn_fwd(qkv, out, lse, B, S, heads)
 
 
 def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads):

@@ -15,6 +15,8 @@ consumed raises (host-side race check).
 """
 from __future__ import annotations
 
+import datetime
+import os
 from collections import deque
 from dataclasses import dataclass, field
 from typing import Deque, List, Optional, Sequence, Tuple
@@ -60,6 +62,11 @@ class Channel:
         self._send_inflight: Deque[Tuple[list, List[torch.Tensor]]] = deque()
         self.sent = 0
         self.received = 0
+        # gloo point-to-point waits have no timeout of their own: bound them here so a lost
+        # message or a dead peer surfaces as an error.  NCCL waits stay stream-level; its
+        # watchdog enforces the process-group timeout.
+        self.host_wait = dist.get_backend(group) == "gloo"
+        self.timeout = datetime.timedelta(seconds=float(os.environ.get("REVPP_P2P_HOST_TIMEOUT_S", "30")))
 
     # -------------------------------------------------------------- receive side
     def _alloc(self):
@@ -93,9 +100,16 @@ class Channel:
             self.post_recv()
         p = self._posted.popleft()
         for w in p.works:
-            w.wait()
+            self._wait(w)
         self.received += 1
         return p.tensors, p.slot
+
+    def _wait(self, w) -> None:
+        if self.host_wait:
+            if not w.wait(self.timeout):
+                raise RuntimeError(f"{self.name}: message not received within {self.timeout}")
+        else:
+            w.wait()
 
     def release(self, slot: int) -> None:
         """The consumer is done with a slot (its reads are enqueued on the current stream)."""
@@ -109,6 +123,11 @@ class Channel:
             if tuple(t.shape) != tuple(s.shape) or t.dtype != s.dtype:
                 raise ValueError(f"{self.name}: message {tuple(t.shape)}/{t.dtype} does not match "
                                  f"{tuple(s.shape)}/{s.dtype}")
+        from .faults import should_drop
+
+        if should_drop(self.name, self.sent):
+            self.sent += 1  # injected loss: the receiver must time out, not hang
+            return
         ops = [dist.P2POp(dist.isend, t, self.dst, self.group) for t in ts]
         works = dist.batch_isend_irecv(ops)
         self._send_inflight.append((works, ts))
@@ -120,20 +139,43 @@ class Channel:
         while len(self._send_inflight) > keep:
             works, _ = self._send_inflight.popleft()
             for w in works:
-                w.wait()
+                self._wait(w)
 
     def drain(self) -> None:
         while self._send_inflight:
             works, _ = self._send_inflight.popleft()
             for w in works:
-                w.wait()
+                self._wait(w)
+
+
+def _warm_group(group, ranks, device) -> None:
+    """Create the group's communicator and, for a two-rank group, its point-to-point
+    connections now.  NCCL builds both on first use, and building them blocks the host
+    until the peer joins; left lazy, stage s would block on its first (early-posted)
+    backward receive before sending its first forward message, while stage s+1 touches
+    the backward channel only after that message arrives.  Warming every group in
+    creation order, with a symmetric send + receive for pairs, cannot deadlock."""
+    me = dist.get_rank()
+    if me not in ranks:
+        return
+    t = torch.zeros(1, device=device)
+    dist.all_reduce(t, group=group)
+    if len(ranks) == 2:
+        peer = ranks[1] if me == ranks[0] else ranks[0]
+        out = torch.zeros(1, device=device)
+        inp = torch.empty(1, device=device)
+        works = dist.batch_isend_irecv([dist.P2POp(dist.isend, out, peer, group),
+                                        dist.P2POp(dist.irecv, inp, peer, group)])
+        for w in works:
+            w.wait()
 
 
 class PipeComms:
     """All channels of one rank: forward/backward to both neighbours plus the label channel.
 
     Process groups are created collectively by every rank in the same order (a requirement
-    of ``new_group``), for every pipeline replica."""
+    of ``new_group``), for every pipeline replica, and their communicators are created
+    eagerly in that order (see ``_warm_group``)."""
 
     def __init__(self, rank: int, world: int, num_stages: int, replicas: int, device: torch.device,
                  fwd_specs, bwd_specs, label_spec: Optional[TensorSpec], depth: int = 2):
@@ -149,7 +191,9 @@ class PipeComms:
             for s in range(num_stages - 1):
                 a, c = b + s, b + s + 1
                 g_f = dist.new_group([a, c], backend=backend)
+                _warm_group(g_f, (a, c), device)
                 g_b = dist.new_group([a, c], backend=backend)
+                _warm_group(g_b, (a, c), device)
                 if d == self.replica:
                     if self.stage == s:
                         self.fwd_out = Channel(f"fwd{s}->{s+1}", a, c, g_f, fwd_specs, device, depth)
@@ -159,6 +203,7 @@ class PipeComms:
                         self.bwd_out = Channel(f"bwd{s+1}->{s}", c, a, g_b, bwd_specs, device, depth)
             if num_stages > 1 and label_spec is not None:
                 g_l = dist.new_group([b, b + num_stages - 1], backend=backend)
+                _warm_group(g_l, (b, b + num_stages - 1), device)
                 if d == self.replica and self.stage in (0, num_stages - 1):
                     self.labels = Channel("labels", b, b + num_stages - 1, g_l, [label_spec], device, depth)
         self.first_rank = base

@@ -16,6 +16,7 @@ from __future__ import annotations
 from typing import List, Optional, Sequence, Tuple
 
 import torch
+import torch.distributed as dist
 
 from .p2p import PipeComms
 
@@ -131,8 +132,12 @@ class PipelineExecutor:
         rem_b = [self.n if bwd_in is not None else 0]
         self._top_up(fwd_in, rem_f)
         self._top_up(bwd_in, rem_b)
+        from .faults import before_forward
+
+        rank = dist.get_rank() if dist.is_initialized() else 0
         for kind, i in acts:
             if kind == "F":
+                before_forward(rank, i)
                 if st.is_first:
                     out = st.forward(i, inputs[i], train)
                 else:

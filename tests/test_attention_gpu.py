@@ -49,3 +49,23 @@ def test_attn_fwd_bwd(B, S, heads):
     err = (dqkv.double() - g).abs().max().item()
     assert err < 3e-2 * (1 + g.abs().max().item()), err
     assert C.status_read_and_clear() == 0
+
+
+@pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3), (1, 2048, 2)])
+def test_attn_fwd_tcgen05(B, S, heads):
+    """tcgen05 forward against float64 attention and against the mma.sync kernel."""
+    C = _C()
+    H = heads * 64
+    qkv = (torch.randn(B * S, 3 * H, device="cuda") * 1.5).to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+    out2 = torch.empty_like(out)
+    lse2 = torch.empty_like(lse)
+    C.attn_fwd(qkv, out2, lse2, B, S, heads)
+    torch.cuda.synchronize()
+    assert C.status_read_and_clear() == 0
+    o_ref, lse_ref = _ref(qkv.double(), B, S, heads)
+    assert (out.double() - o_ref).abs().max().item() < 2e-2
+    assert (lse.double() - lse_ref).abs().max().item() < 2e-3
+    assert (out.double() - out2.double()).abs().max().item() < 2e-2

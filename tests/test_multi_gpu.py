@@ -1,0 +1,51 @@
+"""Multi-GPU tests (NCCL, one process per GPU).  Skipped with fewer than 2 GPUs."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(mode, n=2, timeout=240):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_mgpu_worker.py"), mode]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    res = [json.loads(l[len("RESULT "):]) for l in p.stdout.splitlines() if l.startswith("RESULT ")]
+    return sorted(res, key=lambda r: r["rank"])
+
+
+def test_pipeline_two_stages_matches_single_stage():
+    res = _run("pipeline")
+    r0 = res[0]
+    assert abs(r0["pp_loss"] - r0["single_loss"]) < 2e-2 * max(1.0, abs(r0["single_loss"]))
+    last = res[-1]["losses"]
+    assert all(l == l for l in last)
+    assert all(r["status"] == 0 for r in res)
+
+
+def test_fused_replica_allreduce_matches_nccl():
+    res = _run("dp")
+    for r in res:
+        assert r["fused"] == "FusedP2PReducer"
+        assert r["status"] == 0
+        assert r["max_diff"] <= 1e-3 * max(r["max_step"], 1e-6) + 1e-7, r
+        assert r["replica_diff"] == 0.0
