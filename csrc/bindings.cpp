@@ -10,7 +10,7 @@ namespace revpp {
 void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
              int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
              const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
-             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits);
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant);
 int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K);
 // norm.cu
 void layernorm_fwd(const torch::Tensor& x, const torch::Tensor& gamma, const torch::Tensor& beta, double eps,
@@ -93,7 +93,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &revpp::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("C"),
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("aux_out") = py::none(),
-        py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1);
+        py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1, py::arg("variant") = 0);
   m.def("gemm_suggest_splits", &revpp::gemm_suggest_splits);
 
   m.def("layernorm_fwd", &revpp::layernorm_fwd, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps"),

@@ -338,6 +338,236 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ 2-SM variant
+// A CTA pair (cluster of 2) computes a 256 x 256 tile with tcgen05.mma.cta_group::2:
+// CTA r holds rows [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the
+// B tile (the N half) in shared memory, and receives the 128 x 256 accumulator slice of
+// its A rows in its own TMEM.  Each SM therefore moves 8 KB of operands per 128 x 256 x 16
+// MMA step instead of 12 KB, which keeps the tensor pipe fed.
+//   - both CTAs' TMA loads complete on the leader CTA's `full` barrier (the leader alone
+//     posts the expected byte count); loads carry no multicast;
+//   - the leader's single MMA thread issues the pair's MMAs and commits to `empty`, `tfull`
+//     and `drain` in both CTAs with a multicast commit;
+//   - the leader's `tempty` barrier counts the epilogue warps of both CTAs (the peer's
+//     arrive remotely), so the accumulator is reused only after both halves are read.
+template <int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+  constexpr int BM = 128, BN = 256, BK = kGemmBK;  // per CTA: 128 A rows, 128 B rows; tile 256 x 256
+  constexpr int HALF_N = BN / 2;
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = HALF_N * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull[0], 1);
+    mbar_init(&tfull[1], 1);
+    mbar_init(&tempty[0], 2 * kGemmEpiWarps);
+    mbar_init(&tempty[1], 2 * kGemmEpiWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc2(tmem_slot, TMEM_COLS);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+        const int tm = t % args.tiles_m;
+        const int rest = t / args.tiles_m;
+        const int tn = rest % args.tiles_n;
+        const int ts = rest / args.tiles_n;
+        const int kb0 = ts * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        const int a_row0 = tm * 2 * BM + crank * BM;
+        const int b_row0 = tn * BN + crank * HALF_N;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, abort_flag)) goto producer_abort2;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const uint32_t fb = full_leader0 + stage * 8;
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d_2sm(a_dst, &tmA, fb, kb * BK, a_row0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c) tma_load_2d_2sm(a_dst + c * (BK * 128), &tmA, fb, a_row0 + c * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_2sm(b_dst, &tmB, fb, kb * BK, b_row0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < HALF_N / 64; ++c)
+              tma_load_2d_2sm(b_dst + c * (BK * 128), &tmB, fb, b_row0 + c * 64, kb * BK);
+          }
+          issued |= (1u << stage);
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      goto producer_end2;
+    producer_abort2:
+      // let copies issued by this CTA land (their bytes are counted on the leader's barrier)
+      for (int s = 0; s < STAGES; ++s) {
+        if (leader && (issued & (1u << s))) {
+          const uint32_t par = (issued_parity >> s) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], par) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+      {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    producer_end2:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      const uint32_t a_base = smem_u32(sA);
+      const uint32_t b_base = smem_u32(sB);
+      for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+        const int rest = t / args.tiles_m;
+        const int ts = rest / args.tiles_n;
+        const int kb0 = ts * args.kb_per_split;
+        const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_s = a_base + stage * A_BYTES;
+          const uint32_t b_s = b_base + stage * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_s + k * 2048, BK * 128, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_s + k * 2048, BK * 128, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
+            umma2_bf16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma2_commit_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma2_commit_mc(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma2_commit_mc(drain, 0x3);
+    }
+    if (lane == 0) {
+      // both CTAs: every MMA writing this CTA's TMEM has completed before it is released
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      const int tm = t % args.tiles_m;
+      const int tn = (t / args.tiles_m) % args.tiles_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
+      tc_fence_after();
+      const int row = tm * 2 * BM + crank * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 64; ++c) {
+        const int ccol = half * (BN / 2) + c * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + ccol), r);
+        tmem_wait_ld();
+        gemm_epilogue_chunk<EPI>(args, row, tn * BN + ccol, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, TMEM_COLS);
+  }
+  cluster_sync();
+}
+
 // ------------------------------------------------------------------ host side
 namespace {
 
@@ -355,6 +585,58 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   }
   kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, args);
   REVPP_CHECK_LAUNCH();
+}
+
+template <int STAGES, bool A_MN, bool B_MN, int EPI>
+void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                       cudaStream_t st) {
+  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + 128 * kGemmBK * 2) + 1024 + 256;
+  auto kern = gemm_tc2_kernel<STAGES, A_MN, B_MN, EPI>;
+  static int configured_for = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_for != dev) {
+    REVPP_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured_for = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  REVPP_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  count_launch();
+}
+
+void dispatch_gemm2(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                    const GemmArgs& args, int grid, cudaStream_t st) {
+  constexpr int ST = 6;
+  if (!a_mn && !b_mn) {
+    switch (epi) {
+      case kEpiBF16: return launch_gemm2_inst<ST, false, false, kEpiBF16>(ta, tb, args, grid, st);
+      case kEpiGelu: return launch_gemm2_inst<ST, false, false, kEpiGelu>(ta, tb, args, grid, st);
+      case kEpiResid: return launch_gemm2_inst<ST, false, false, kEpiResid>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm2_inst<ST, false, false, kEpiF32>(ta, tb, args, grid, st);
+      default: break;
+    }
+  } else if (!a_mn && b_mn) {
+    switch (epi) {
+      case kEpiBF16: return launch_gemm2_inst<ST, false, true, kEpiBF16>(ta, tb, args, grid, st);
+      case kEpiDGelu: return launch_gemm2_inst<ST, false, true, kEpiDGelu>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm2_inst<ST, false, true, kEpiF32>(ta, tb, args, grid, st);
+      default: break;
+    }
+  } else if (a_mn && b_mn) {
+    if (epi == kEpiAtomicF32) return launch_gemm2_inst<ST, true, true, kEpiAtomicF32>(ta, tb, args, grid, st);
+  }
+  REVPP_CHECK(false, "2-SM GEMM layout/epilogue combination not built: a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 }
 
 // Only the operand-layout / epilogue pairs the models use are instantiated:
@@ -389,10 +671,11 @@ void dispatch_gemm(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const C
 
 // A: if !a_mn, [M, K] row-major (row stride lda); if a_mn, [K, M] row-major.
 // B: if !b_mn, [N, K] row-major; if b_mn, [K, N] row-major.
+// variant: 0 = automatic (2-SM kernel unless M <= 128), 1 = one-CTA kernel, 2 = 2-SM kernel.
 void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
              int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
              const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
-             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits) {
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant) {
   check_cuda_bf16(A, "A");
   check_cuda_bf16(B, "B");
   REVPP_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm operands must be 2-D");
@@ -421,11 +704,13 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
   REVPP_CHECK(splits == 1 || epi == kEpiAtomicF32, "split-K needs the atomic epilogue");
   c10::cuda::CUDAGuard guard(A.device());
 
+  const bool two_sm = variant == 2 || (variant == 0 && M > kGemmBM);
+  const int tile_m = two_sm ? 2 * kGemmBM : kGemmBM;
   GemmArgs args{};
   args.M = static_cast<int>(M);
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
-  args.tiles_m = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  args.tiles_m = static_cast<int>((M + tile_m - 1) / tile_m);
   args.tiles_n = static_cast<int>((N + 255) / 256);
   args.kb_total = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
   const int want_splits = static_cast<int>(std::min<int64_t>(splits, args.kb_total));
@@ -473,18 +758,24 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
   CUtensorMap ta, tb;
   if (!a_mn) ta = make_tmap_2d(A.data_ptr(), bf, 2, K, M, A.stride(0) * 2, 64, kGemmBM, sw);
   else ta = make_tmap_2d(A.data_ptr(), bf, 2, M, K, A.stride(0) * 2, 64, kGemmBK, sw);
-  if (!b_mn) tb = make_tmap_2d(B.data_ptr(), bf, 2, K, N, B.stride(0) * 2, 64, 256, sw);
+  if (!b_mn) tb = make_tmap_2d(B.data_ptr(), bf, 2, K, N, B.stride(0) * 2, 64, two_sm ? 128 : 256, sw);
   else tb = make_tmap_2d(B.data_ptr(), bf, 2, N, K, B.stride(0) * 2, 64, kGemmBK, sw);
 
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
-  const int grid = std::min(num_tiles, gemm_grid_sms());
   cudaStream_t st = cur_stream();
-  dispatch_gemm(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, grid, st);
+  if (two_sm) {
+    const int clusters = std::max(1, std::min(num_tiles, gemm_grid_sms() / 2));
+    dispatch_gemm2(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, 2 * clusters, st);
+  } else {
+    const int grid = std::min(num_tiles, gemm_grid_sms());
+    dispatch_gemm(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, grid, st);
+  }
 }
 
 // Split count that fills the machine for the weight-gradient GEMM.
 int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + 255) / 256);
+  // 2-SM tiles are 256 x 256 and occupy two SMs each
+  const int64_t tiles = 2 * ((M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((N + 255) / 256);
   const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
   const int64_t sms = num_sms();
   int64_t s = std::max<int64_t>(1, sms / std::max<int64_t>(tiles, 1));

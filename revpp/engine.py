@@ -90,12 +90,10 @@ class Trainer:
         self.pp_group = None
         if dist.is_initialized():
             label_spec = TensorSpec((self.local_batch,), torch.int64)
-            bwd = self.stage.bwd_specs(self.stage_index)
-            self.comms = PipeComms(self.rank, world, self.P, self.D, self.device, self.stage.fwd_specs(), bwd,
-                                   label_spec)
-            # the bwd channel into this stage carries the next stage's message layout
-            if self.comms.bwd_in is not None:
-                self.comms.bwd_in.specs = self.stage.bwd_specs(self.stage_index)
+            # messages into this stage: the previous stage's outputs, and the next stage's
+            # backward message for this receiver
+            self.comms = PipeComms(self.rank, world, self.P, self.D, self.device, self.stage.fwd_specs(),
+                                   self.stage.bwd_specs(self.stage_index), label_spec)
             from revpp.parallel.p2p import _warm_group
 
             if self.D > 1:
@@ -106,12 +104,7 @@ class Trainer:
                     if s == self.stage_index:
                         self.dp_group = g
             if self.P > 1:
-                for d in range(self.D):
-                    ranks = list(range(d * self.P, (d + 1) * self.P))
-                    g = dist.new_group(ranks)
-                    _warm_group(g, ranks, self.device)
-                    if d == self.replica:
-                        self.pp_group = g
+                self.pp_group = self.comms.group
         if self.P > 1 and self.device.type == "cuda":
             from revpp import ops
 

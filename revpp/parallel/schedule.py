@@ -1,15 +1,13 @@
 """Pipeline schedules as explicit per-rank action lists, and their executor.
 
 ``one_f_one_b(stage, P, n)`` gives the reference's Schedule1F1B order
-(BERT/pipelining/schedules.py:677-852): min(P - s - 1, n) warm-up forwards, then
+(BERT/pipelining/schedules.py:677-852): min(P - s, n) warm-up forwards, then
 alternating forward / backward, then the remaining backwards.  ``gpipe`` is all forwards
 then all backwards (ScheduleGPipe, schedules.py:591-673); ``forward_only`` is the
 evaluation schedule (_ScheduleForwardOnly, schedules.py:538-588).
 
-The executor posts receives ahead of use (depth-2 ring per channel), so the transfer
-of micro-batch k+1 overlaps the compute of micro-batch k; each wait is a stream-level
-dependency, not a host block.  Labels travel from the first to the last stage once per
-step, as in the reference engine (BERT/src/engine.py:174-176, 238-240).
+Labels travel from the first to the last stage once per step, as in the reference engine
+(BERT/src/engine.py:174-176, 238-240).
 """
 from __future__ import annotations
 
@@ -24,7 +22,7 @@ Action = Tuple[str, int]
 
 
 def one_f_one_b(stage: int, num_stages: int, n: int) -> List[Action]:
-    warmup = min(num_stages - stage - 1, n)
+    warmup = min(num_stages - stage, n)
     acts: List[Action] = [("F", i) for i in range(warmup)]
     f, b = warmup, 0
     while f < n:
@@ -90,6 +88,17 @@ def simulate(num_stages: int, n: int, schedule: str = "1f1b", t_f: float = 1.0, 
 
 
 class PipelineExecutor:
+    """Runs a schedule on one rank.  Communication follows the reference's grouping
+    (BERT/pipelining/schedules.py:700-852) on a single process group per pipeline:
+
+      warm-up (min(n, P - s) forwards): receive input -> forward -> send output; the last
+        warm-up send is held back and grouped with the first backward receive;
+      steady state: [forward send + backward receive] -> backward ->
+                    [backward send + forward receive] -> forward;
+      cool-down: backward receive -> backward -> backward send.
+
+    Waits are stream-level on NCCL.  Receive buffers come from the rings in ``PipeComms``."""
+
     def __init__(self, stage, comms: Optional[PipeComms], num_microbatches: int, schedule: str = "1f1b"):
         self.stage = stage
         self.comms = comms
@@ -98,14 +107,53 @@ class PipelineExecutor:
         self.P = stage.num_stages
         self.s = stage.stage_index
 
-    def _top_up(self, ch, remaining: List[int]) -> None:
-        """Keep up to ``depth`` receives posted on a channel."""
-        if ch is None:
-            return
-        while remaining[0] > 0 and ch.posted < ch.depth and not ch._slot_busy[ch._next_slot]:
-            ch.post_recv()
-            remaining[0] -= 1
+    # ---------------------------------------------------------------- helpers
+    def _rank(self) -> int:
+        return dist.get_rank() if dist.is_initialized() else 0
 
+    def _recv_fwd(self):
+        if self.stage.is_first:
+            return [], None
+        return self.comms.recv_fwd()
+
+    def _recv_bwd(self):
+        if self.stage.is_last:
+            return [], None
+        return self.comms.recv_bwd()
+
+    def _forward(self, i, meta, inputs, train):
+        from .faults import before_forward
+
+        before_forward(self._rank(), i)
+        x = inputs[i] if meta is None else meta[2]
+        out = self.stage.forward(i, x, train)
+        if meta is not None:
+            meta[0].release(meta[1])
+        return out
+
+    def _backward(self, i, meta):
+        g = self.stage.backward(i, None if meta is None else meta[2])
+        if meta is not None:
+            meta[0].release(meta[1])
+        return g
+
+    def _send_fwd(self, out):
+        if out is None or self.stage.is_last or self.comms is None:
+            return [], []
+        return self.comms.send_fwd(out)
+
+    def _send_bwd(self, g):
+        if g is None or self.stage.is_first or self.comms is None:
+            return [], []
+        return self.comms.send_bwd(g)
+
+    def _run(self, ops, keep=()):
+        cm = self.comms
+        if cm is None or not ops:
+            return
+        cm.wait(cm.issue(ops, list(keep)))
+
+    # ---------------------------------------------------------------- entry
     def step(self, inputs: Optional[Sequence] = None, labels: Optional[torch.Tensor] = None,
              train: bool = True):
         """Run one global batch through the pipeline.  ``inputs``: per-micro-batch inputs of the
@@ -114,47 +162,94 @@ class PipelineExecutor:
         st = self.stage
         cm = self.comms
         st.clear()
-        # labels: first -> last
-        if self.P > 1 and cm is not None and cm.labels is not None:
-            if st.is_first and labels is not None:
-                cm.labels.send([labels])
+        if self.P > 1 and cm is not None:
+            ops, buf = cm.labels_ops(labels, st.is_first, st.is_last)
+            self._run(ops, [buf] if buf is not None else [])
             if st.is_last:
-                (lab,), slot = cm.labels.recv()
-                labels = lab.clone()
-                cm.labels.release(slot)
+                labels = buf
         if st.is_last:
             st.labels = list(torch.tensor_split(labels, self.n)) if labels is not None else None
-        fn = SCHEDULES[self.schedule] if train else forward_only
-        acts = fn(self.s, self.P, self.n)
-        fwd_in = cm.fwd_in if cm is not None else None
-        bwd_in = cm.bwd_in if (cm is not None and train) else None
-        rem_f = [self.n if fwd_in is not None else 0]
-        rem_b = [self.n if bwd_in is not None else 0]
-        self._top_up(fwd_in, rem_f)
-        self._top_up(bwd_in, rem_b)
-        from .faults import before_forward
-
-        rank = dist.get_rank() if dist.is_initialized() else 0
-        for kind, i in acts:
-            if kind == "F":
-                before_forward(rank, i)
-                if st.is_first:
-                    out = st.forward(i, inputs[i], train)
-                else:
-                    msg, slot = fwd_in.recv()
-                    out = st.forward(i, msg, train)
-                    fwd_in.release(slot)
-                    self._top_up(fwd_in, rem_f)
-                if out is not None and cm is not None and cm.fwd_out is not None:
-                    cm.fwd_out.send(out)
-            else:
-                if st.is_last:
-                    g = st.backward(i, None)
-                else:
-                    msg, slot = bwd_in.recv()
-                    g = st.backward(i, msg)
-                    bwd_in.release(slot)
-                    self._top_up(bwd_in, rem_b)
-                if g is not None and cm is not None and cm.bwd_out is not None:
-                    cm.bwd_out.send(g)
+        if not train:
+            self._forward_pass(inputs, train=False)
+        elif self.schedule == "gpipe":
+            self._forward_pass(inputs, train=True)
+            self._backward_pass()
+        else:
+            self._one_f_one_b(inputs)
         return st.losses
+
+    def _forward_pass(self, inputs, train: bool):
+        cm = self.comms
+        send_h = None
+        for i in range(self.n):
+            ops, meta = self._recv_fwd()
+            self._run(ops)
+            out = self._forward(i, meta, inputs, train)
+            if cm is not None:
+                cm.wait(send_h)
+                sops, keep = self._send_fwd(out)
+                send_h = cm.issue(sops, keep)
+        if cm is not None:
+            cm.wait(send_h)
+
+    def _backward_pass(self):
+        cm = self.comms
+        send_h = None
+        for i in range(self.n):
+            ops, meta = self._recv_bwd()
+            self._run(ops)
+            g = self._backward(i, meta)
+            if cm is not None:
+                cm.wait(send_h)
+                sops, keep = self._send_bwd(g)
+                send_h = cm.issue(sops, keep)
+        if cm is not None:
+            cm.wait(send_h)
+
+    def _one_f_one_b(self, inputs):
+        cm = self.comms
+        n = self.n
+        warmup = min(n, self.P - self.s)
+        fi = bi = 0
+        send_h = None
+        fsend_ops, fsend_keep = [], []
+        for _ in range(warmup):
+            ops, meta = self._recv_fwd()
+            self._run(ops)
+            out = self._forward(fi, meta, inputs, True)
+            if cm is not None:
+                cm.wait(send_h)
+                send_h = None
+            fsend_ops, fsend_keep = self._send_fwd(out)
+            if fi != warmup - 1 and cm is not None:
+                send_h = cm.issue(fsend_ops, fsend_keep)
+                fsend_ops, fsend_keep = [], []
+            fi += 1
+        bsend_ops, bsend_keep = [], []
+        while True:
+            ops, meta = self._recv_bwd()
+            self._run(fsend_ops + ops, fsend_keep)
+            fsend_ops, fsend_keep = [], []
+            g = self._backward(bi, meta)
+            bsend_ops, bsend_keep = self._send_bwd(g)
+            bi += 1
+            if fi == n:
+                break
+            ops, meta = self._recv_fwd()
+            self._run(bsend_ops + ops, bsend_keep)
+            bsend_ops, bsend_keep = [], []
+            out = self._forward(fi, meta, inputs, True)
+            fsend_ops, fsend_keep = self._send_fwd(out)
+            fi += 1
+        send_h = cm.issue(bsend_ops, bsend_keep) if cm is not None else None
+        while bi < n:
+            ops, meta = self._recv_bwd()
+            self._run(ops)
+            g = self._backward(bi, meta)
+            if cm is not None:
+                cm.wait(send_h)
+            bsend_ops, bsend_keep = self._send_bwd(g)
+            send_h = cm.issue(bsend_ops, bsend_keep) if cm is not None else None
+            bi += 1
+        if cm is not None:
+            cm.wait(send_h)

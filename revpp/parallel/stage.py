@@ -189,7 +189,8 @@ class StandardStage(StageBase):
         return x, ctxs
 
     def forward(self, mb, inputs, train=True):
-        x = self._embed(mb, inputs) if self.is_first else inputs[0]
+        # the received buffer belongs to a receive ring; keep a copy when it must outlive this call
+        x = self._embed(mb, inputs) if self.is_first else (inputs[0].clone() if train else inputs[0])
         y, ctxs = self._run(x, save=train)
         if train:
             self.ctx_cache[mb] = ctxs
@@ -227,7 +228,7 @@ class CheckpointStage(StandardStage):
             return super().forward(mb, inputs, train)
         x = self._embed(mb, inputs) if self.is_first else inputs[0]
         if train and not self.is_first:
-            self.input_cache[mb] = (x,)
+            self.input_cache[mb] = (x.clone(),)  # the receive ring reuses its buffers
         y, _ = self._run(x, save=False)
         return (y,)
 

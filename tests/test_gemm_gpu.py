@@ -31,39 +31,42 @@ def _close(out, ref, rtol):
     assert err <= rtol * scale, f"max abs err {err} vs scale {scale}"
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_fwd_bias_bf16(M, N, K):
+def test_fwd_bias_bf16(M, N, K, variant):
     C = _C()
     a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    C.gemm_tc(a, False, b, False, M, N, K, EPI_BF16, out, bias=bias)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_BF16, out, bias=bias, variant=variant)
     torch.cuda.synchronize()
     assert C.status_read_and_clear() == 0
     ref = a.double() @ b.double().t() + bias.double()
     _close(out, ref, 1e-2)
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_fwd_gelu(M, N, K):
+def test_fwd_gelu(M, N, K, variant):
     C = _C()
     a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    C.gemm_tc(a, False, b, False, M, N, K, EPI_GELU, out, bias=bias, aux_out=pre)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_GELU, out, bias=bias, aux_out=pre, variant=variant)
     torch.cuda.synchronize()
     u = a.double() @ b.double().t() + bias.double()
     _close(pre, u, 1e-2)
     _close(out, _gelu(pre.double()), 1e-2)
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("sign", [1.0, -1.0])
-def test_fwd_resid(M, N, K, sign):
+def test_fwd_resid(M, N, K, sign, variant):
     C = _C()
     a, b, bias = _rand(M, K), _rand(N, K, scale=0.05), _rand(N, scale=0.1)
     resid = torch.randn(M, N, device="cuda")
     out = torch.empty(M, N, device="cuda")
-    C.gemm_tc(a, False, b, False, M, N, K, EPI_RESID, out, bias=bias, resid=resid, sign=sign)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_RESID, out, bias=bias, resid=resid, sign=sign, variant=variant)
     torch.cuda.synchronize()
     f = (a.float() @ b.float().t() + bias.float()).to(torch.bfloat16).double()
     ref = resid.double() + sign * f
@@ -71,24 +74,26 @@ def test_fwd_resid(M, N, K, sign):
     _close(out, ref, 1e-2)
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_dgrad_mn(M, N, K):
+def test_dgrad_mn(M, N, K, variant):
     """C[M,N] = A[M,K] @ W where W is stored [K, N] (MN-major B)."""
     C = _C()
     a, w = _rand(M, K), _rand(K, N, scale=0.05)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    C.gemm_tc(a, False, w, True, M, N, K, EPI_BF16, out)
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_BF16, out, variant=variant)
     torch.cuda.synchronize()
     _close(out, a.double() @ w.double(), 1e-2)
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_dgelu(M, N, K):
+def test_dgelu(M, N, K, variant):
     C = _C()
     a, w = _rand(M, K), _rand(K, N, scale=0.05)
     u = _rand(M, N)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u)
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u, variant=variant)
     torch.cuda.synchronize()
     ud = u.double()
     dg = 0.5 * (1 + torch.erf(ud / math.sqrt(2))) + ud * torch.exp(-0.5 * ud * ud) / math.sqrt(2 * math.pi)
@@ -99,25 +104,27 @@ def test_dgelu(M, N, K):
 WGRAD_SHAPES = [(128, 256, 64), (256, 512, 256), (96, 160, 197 * 3), (1024, 1024, 1000), (3072, 1024, 4096)]
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", WGRAD_SHAPES)
 @pytest.mark.parametrize("splits", [1, 3])
-def test_wgrad_atomic(M, N, K, splits):
+def test_wgrad_atomic(M, N, K, splits, variant):
     """C[M,N] += A^T B where A stored [K, M] and B stored [K, N] (both MN-major)."""
     C = _C()
     a, b = _rand(K, M), _rand(K, N)
     out = torch.randn(M, N, device="cuda")
     ref = out.double() + a.double().t() @ b.double()
-    C.gemm_tc(a, True, b, True, M, N, K, EPI_ATOMIC, out, splits=splits)
+    C.gemm_tc(a, True, b, True, M, N, K, EPI_ATOMIC, out, splits=splits, variant=variant)
     torch.cuda.synchronize()
     _close(out, ref, 1e-4)
 
 
-def test_fwd_f32_persistent_many_tiles():
+@pytest.mark.parametrize("variant", [1, 2])
+def test_fwd_f32_persistent_many_tiles(variant):
     C = _C()
     M, N, K = 8192, 4096, 512
     a, b = _rand(M, K), _rand(N, K, scale=0.05)
     out = torch.empty(M, N, device="cuda")
-    C.gemm_tc(a, False, b, False, M, N, K, EPI_F32, out)
+    C.gemm_tc(a, False, b, False, M, N, K, EPI_F32, out, variant=variant)
     torch.cuda.synchronize()
     _close(out, a.float() @ b.float().t(), 1e-4)
     assert C.status_read_and_clear() == 0
