@@ -467,6 +467,25 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bf
 }
 
 // ------------------------------------------------------------------ host side
+void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, int64_t M, int64_t S,
+                         int64_t heads) {
+  const long long warps = M * heads;
+  const int threads = 256;
+  const long long blocks = (warps * 32 + threads - 1) / threads;
+  attn_bwd_dot_kernel<<<static_cast<unsigned>(blocks), threads, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+      D.data_ptr<float>(), static_cast<int>(M), static_cast<int>(S), static_cast<int>(heads));
+  REVPP_CHECK_LAUNCH();
+}
+
+void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H) {
+  const long long n4 = M * H / 4;
+  const int threads = 256;
+  attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + threads - 1) / threads), threads, 0, cur_stream()>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), M, static_cast<int>(H));
+  REVPP_CHECK_LAUNCH();
+}
+
 void attn_fwd(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S, int64_t heads) {
   check_cuda_bf16(qkv, "qkv");
   check_cuda_bf16(out, "out");

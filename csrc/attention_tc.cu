@@ -344,4 +344,393 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
   REVPP_CHECK_LAUNCH();
 }
 
+
+// ====================================================================== backward
+// Flash attention backward on tcgen05.  One CTA per (key tile of 128, head, sequence);
+// the CTA walks the query tiles (128 queries each):
+//   S^T  = K Q_j^T      (M 128 keys, N 128 queries, K 64)   -> TMEM cols [0, 128)
+//   dP^T = V dO_j^T     (same shape)                         -> TMEM cols [128, 256)
+//   softmax warps (one thread per key): P^T = exp(S^T * scale - lse_q),
+//       dS^T = P^T * (dP^T - D_q), both bf16 into 128-byte-swizzled smem tiles
+//   dV  += P^T dO_j     (M 128 keys, N 64, K 128 queries)   -> TMEM cols [256, 320)
+//   dK  += dS^T Q_j     (same)                               -> TMEM cols [320, 384)
+//   dQ_j = dS K         (M 128 queries, N 64, K 128 keys; dS read MN-major from the dS^T
+//                        tile)                               -> TMEM cols [384, 448)
+//   dQ warps (one thread per query) add dQ_j * scale into an fp32 buffer with atomics.
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax / final dK dV, 6-9 dQ.
+namespace {
+constexpr int kBK = 128;  // keys per CTA
+constexpr int kBQ = 128;  // queries per tile
+constexpr int kBwdThreads = 320;
+constexpr uint32_t kTile = 128 * 64 * 2;       // 16 KB: a [128 x 64] bf16 tile
+constexpr uint32_t kSqTile = 2 * kTile;        // 32 KB: a [128 x 128] bf16 tile (2 swizzle chunks)
+struct BwdSmem {
+  static constexpr uint32_t k = 0;
+  static constexpr uint32_t v = k + kTile;
+  static constexpr uint32_t q = v + kTile;          // 2 buffers
+  static constexpr uint32_t dout = q + 2 * kTile;   // 2 buffers
+  static constexpr uint32_t pt = dout + 2 * kTile;  // P^T
+  static constexpr uint32_t dst = pt + kSqTile;     // dS^T
+  static constexpr uint32_t stats = dst + kSqTile;  // lse*log2e [2][128], D [2][128]
+  static constexpr uint32_t bars = stats + 4 * 128 * 4;
+  static constexpr uint32_t total = bars + 256;
+};
+constexpr uint32_t kIdescSq = idesc_bf16(128, 128, false, false);
+constexpr uint32_t kIdescKD = idesc_bf16(128, 64, false, true);
+constexpr uint32_t kIdescQD = idesc_bf16(128, 64, true, true);
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+}  // namespace
+
+struct AttnBwdTcArgs {
+  const float* lse;   // [B, heads, S]
+  const float* D;     // [B, heads, S]
+  float* dq_acc;      // [B*S, H] fp32, zeroed
+  __nv_bfloat16* dqkv;
+  int S, heads;
+  float scale, scale_log2;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
+                       const AttnBwdTcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + BwdSmem::bars);
+  uint64_t* kv_full = bar + 0;
+  uint64_t* q_full = bar + 1;     // [2]
+  uint64_t* q_empty = bar + 3;    // [2]
+  uint64_t* s_full = bar + 5;
+  uint64_t* s_empty = bar + 6;
+  uint64_t* p_full = bar + 7;
+  uint64_t* p_empty = bar + 8;
+  uint64_t* dq_full = bar + 9;
+  uint64_t* dq_empty = bar + 10;
+  uint64_t* kv_done = bar + 11;
+  uint64_t* drain = bar + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [2][128]
+  float* s_D = s_lse + 2 * 128;                                        // [2][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int S = args.S;
+  const int H = args.heads * 64;
+  const int row0 = b * S;
+  const int k0 = kt * kBK;
+  const int nq = (S + kBQ - 1) / kBQ;
+  const float* g_lse = args.lse + (static_cast<long long>(b) * args.heads + h) * S;
+  const float* g_D = args.D + (static_cast<long long>(b) * args.heads + h) * S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(kv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQKV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- producer
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      tma_load_2d(smem + BwdSmem::k, &tmQKV, kv_full, H + h * 64, row0 + k0);
+      tma_load_2d(smem + BwdSmem::v, &tmQKV, kv_full, 2 * H + h * 64, row0 + k0);
+      uint32_t issued = 0, issued_par = 0;
+      for (int j = 0; j < nq; ++j) {
+        const int bb = j & 1;
+        const uint32_t par = (j >> 1) & 1;
+        if (!mbar_wait(&q_empty[bb], par ^ 1u, args.status, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[bb], 2 * kTile);
+        tma_load_2d(smem + BwdSmem::q + bb * kTile, &tmQKV, &q_full[bb], h * 64, row0 + j * kBQ);
+        tma_load_2d(smem + BwdSmem::dout + bb * kTile, &tmDO, &q_full[bb], h * 64, row0 + j * kBQ);
+        issued |= 1u << bb;
+        issued_par = (issued_par & ~(1u << bb)) | (par << bb);
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+        for (int s = 0; s < 2; ++s) {
+          if (!(issued & (1u << s))) continue;
+          const uint64_t t1 = globaltimer_ns();
+          while (!mbar_try_wait(&q_full[s], (issued_par >> s) & 1u) && globaltimer_ns() - t1 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      const uint32_t a_k = smem_u32(smem + BwdSmem::k);
+      const uint32_t a_v = smem_u32(smem + BwdSmem::v);
+      const uint32_t a_q = smem_u32(smem + BwdSmem::q);
+      const uint32_t a_do = smem_u32(smem + BwdSmem::dout);
+      const uint32_t a_pt = smem_u32(smem + BwdSmem::pt);
+      const uint32_t a_ds = smem_u32(smem + BwdSmem::dst);
+      bool ok = mbar_wait(kv_full, 0, args.status, abort_flag);
+      for (int j = 0; ok && j < nq; ++j) {
+        const int bb = j & 1;
+        const uint32_t par = (j >> 1) & 1;
+        const uint32_t jp = j & 1;
+        if (!mbar_wait(&q_full[bb], par, args.status, abort_flag)) break;
+        if (!mbar_wait(s_empty, jp ^ 1u, args.status, abort_flag)) break;
+        tc_fence_after();
+        // S^T = K Q^T ; dP^T = V dO^T
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          umma_bf16_ss(tmem, sdesc_sw128(a_k + k * 32, 16, 1024), sdesc_sw128(a_q + bb * kTile + k * 32, 16, 1024),
+                       kIdescSq, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          umma_bf16_ss(tmem + 128, sdesc_sw128(a_v + k * 32, 16, 1024),
+                       sdesc_sw128(a_do + bb * kTile + k * 32, 16, 1024), kIdescSq, k > 0);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
+        if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ka = (k >> 2) * kTile + (k & 3) * 32;   // K-major over queries (2 chunks)
+          // dV += P^T dO   (B = dO, MN-major: d contiguous, queries as K rows)
+          umma_bf16_ss(tmem + 256, sdesc_sw128(a_pt + ka, 16, 1024),
+                       sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
+          // dK += dS^T Q
+          umma_bf16_ss(tmem + 320, sdesc_sw128(a_ds + ka, 16, 1024),
+                       sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          // dQ = dS K : A = dS (queries contiguous in the dS^T tile -> MN-major, 64-query
+          // chunks 16 KB apart), B = K (MN-major: d contiguous, keys as K rows)
+          umma_bf16_ss(tmem + 384, sdesc_sw128(a_ds + k * 2048, kTile, 1024), sdesc_sw128(a_k + k * 2048, 8192, 1024),
+                       kIdescQD, k > 0);
+        }
+        umma_commit(dq_full);
+        umma_commit(p_empty);
+        umma_commit(&q_empty[bb]);
+      }
+      umma_commit(kv_done);
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------------ softmax (keys)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;      // key row within the tile
+    const int tid = r;                      // 0..127 within this warpgroup
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool key_ok = k0 + r < S;
+    const float ln2inv = 1.4426950408889634f;
+    uint8_t* pt_base = smem + BwdSmem::pt;
+    uint8_t* ds_base = smem + BwdSmem::dst;
+    bool ok = true;
+    for (int j = 0; j < nq; ++j) {
+      const int bb = j & 1;
+      const uint32_t jp = j & 1;
+      const int qi = j * kBQ + tid;
+      s_lse[bb * 128 + tid] = qi < S ? g_lse[qi] * ln2inv : 0.f;
+      s_D[bb * 128 + tid] = qi < S ? g_D[qi] : 0.f;
+      named_bar_sync(1, 128);
+      if (!mbar_wait(s_full, jp, args.status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (!mbar_wait(p_empty, jp ^ 1u, args.status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int sw = r & 7;
+      uint8_t* prow = pt_base + (r >> 3) * 1024 + sw * 128;
+      uint8_t* drow = ds_base + (r >> 3) * 1024 + sw * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dp[32];
+        tmem_ld32(tmem + lane_off + c * 32, sv);
+        tmem_ld32(tmem + lane_off + 128 + c * 32, dp);
+        tmem_wait_ld();
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int ql0 = c * 32 + e;
+          const bool v0 = key_ok && (j * kBQ + ql0 < S);
+          const bool v1 = key_ok && (j * kBQ + ql0 + 1 < S);
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[e]) * args.scale_log2 - s_lse[bb * 128 + ql0]) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[e + 1]) * args.scale_log2 - s_lse[bb * 128 + ql0 + 1]) : 0.f;
+          const uint32_t pp = pack_bf16x2(p0, p1);
+          const float2 pr = unpack_bf16x2(pp);
+          const float d0 = pr.x * (__uint_as_float(dp[e]) - s_D[bb * 128 + ql0]);
+          const float d1 = pr.y * (__uint_as_float(dp[e + 1]) - s_D[bb * 128 + ql0 + 1]);
+          pw[e >> 1] = pp;
+          dw[e >> 1] = pack_bf16x2(d0, d1);
+        }
+        // 32 queries = 64 bytes = four 16-byte units of the row, in chunk c >> 1
+        const int chunk = c >> 1;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int u = (c & 1) * 4 + t;
+          const uint32_t off = chunk * kTile + ((u ^ sw) << 4);
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * t], pw[4 * t + 1], pw[4 * t + 2], pw[4 * t + 3]);
+          *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(p_full);
+        mbar_arrive(s_empty);
+      }
+    }
+    // final dK, dV for this warp's keys
+    if (ok && mbar_wait(kv_done, 0, args.status, abort_flag)) {
+      tc_fence_after();
+      uint32_t dv[2][32], dk[2][32];
+      tmem_ld32(tmem + lane_off + 256, dv[0]);
+      tmem_ld32(tmem + lane_off + 288, dv[1]);
+      tmem_ld32(tmem + lane_off + 320, dk[0]);
+      tmem_ld32(tmem + lane_off + 352, dk[1]);
+      tmem_wait_ld();
+      if (key_ok) {
+        const long long ld = 3LL * H;
+        uint4* gk = reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + k0 + r) * ld + H + h * 64);
+        uint4* gv = reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + k0 + r) * ld + 2 * H + h * 64);
+        const float sc = args.scale;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c0 = 8 * u;
+          uint32_t kw[4], vw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int cc = c0 + 2 * e;
+            kw[e] = pack_bf16x2(__uint_as_float(dk[cc >> 5][cc & 31]) * sc, __uint_as_float(dk[(cc + 1) >> 5][(cc + 1) & 31]) * sc);
+            vw[e] = pack_bf16x2(__uint_as_float(dv[cc >> 5][cc & 31]), __uint_as_float(dv[(cc + 1) >> 5][(cc + 1) & 31]));
+          }
+          gk[u] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+          gv[u] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ dQ (queries)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int j = 0; j < nq; ++j) {
+      if (!mbar_wait(dq_full, j & 1, args.status, abort_flag)) break;
+      tc_fence_after();
+      uint32_t dq[2][32];
+      tmem_ld32(tmem + lane_off + 384, dq[0]);
+      tmem_ld32(tmem + lane_off + 416, dq[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      const int q = j * kBQ + r;
+      if (q < S) {
+        float* dst = args.dq_acc + (static_cast<long long>(row0) + q) * H + h * 64;
+        const float sc = args.scale;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int cc = 4 * u;
+          atomicAdd(reinterpret_cast<float4*>(dst + cc),
+                    make_float4(__uint_as_float(dq[cc >> 5][cc & 31]) * sc, __uint_as_float(dq[cc >> 5][(cc & 31) + 1]) * sc,
+                                __uint_as_float(dq[cc >> 5][(cc & 31) + 2]) * sc,
+                                __uint_as_float(dq[cc >> 5][(cc & 31) + 3]) * sc));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, int64_t M, int64_t S,
+                         int64_t heads);
+void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H);
+
+void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
+                 const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
+                 int64_t S, int64_t heads) {
+  check_cuda_bf16(qkv, "qkv");
+  check_cuda_bf16(out, "out");
+  check_cuda_bf16(dout, "dout");
+  check_cuda_bf16(dqkv, "dqkv");
+  check_cuda_f32(lse, "lse");
+  check_cuda_f32(dq_acc, "dq_acc");
+  check_cuda_f32(Dbuf, "D");
+  const int64_t H = heads * 64;
+  const int64_t M = B * S;
+  REVPP_CHECK(qkv.is_contiguous() && qkv.size(0) == M && qkv.size(1) == 3 * H, "qkv must be [B*S, 3H]");
+  REVPP_CHECK(dqkv.is_contiguous() && dqkv.size(0) == M && dqkv.size(1) == 3 * H, "dqkv must be [B*S, 3H]");
+  REVPP_CHECK(dout.is_contiguous() && dout.numel() == M * H && out.numel() == M * H, "out/dout must be [B*S, H]");
+  REVPP_CHECK(dq_acc.numel() >= M * H && Dbuf.numel() >= B * heads * S, "scratch too small");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  cudaStream_t st = cur_stream();
+  REVPP_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, M * H * sizeof(float), st));
+  attn_bwd_dot_launch(dout, out, Dbuf, M, S, heads);
+  const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMap tq = make_tmap_2d(qkv.data_ptr(), bf, 2, 3 * H, M, 3 * H * 2, 64, 128, sw);
+  const CUtensorMap tdo = make_tmap_2d(dout.data_ptr(), bf, 2, H, M, H * 2, 64, 128, sw);
+  AttnBwdTcArgs a;
+  a.lse = lse.data_ptr<float>();
+  a.D = Dbuf.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.S = static_cast<int>(S);
+  a.heads = static_cast<int>(heads);
+  a.scale = static_cast<float>(1.0 / std::sqrt(64.0));
+  a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
+  a.status = status_device_ptr();
+  constexpr int smem = BwdSmem::total + 1024;
+  static int configured_for = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_for != dev) {
+    REVPP_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured_for = dev;
+  }
+  dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, smem, st>>>(tq, tdo, a);
+  REVPP_CHECK_LAUNCH();
+  attn_dq_convert_launch(dq_acc, dqkv, M, H);
+}
+
 }  // namespace revpp

@@ -45,6 +45,10 @@ void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<in
                      double beta1, double beta2, double eps, double wd, int64_t step, double max_norm,
                      double timeout_s, bool zero_grad);
 void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch::Tensor result);
+std::vector<int64_t> pointer_info(int64_t ptr);
+void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
+                 const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
+                 int64_t S, int64_t heads);
 // embed_head.cu
 void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
                     const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
@@ -106,6 +110,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("heads"));
   m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("heads"));
+  m.def("attn_bwd_tc", &revpp::attn_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
+        py::arg("dqkv"), py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
         py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("bert_embed_fwd", &revpp::bert_embed_fwd);
@@ -124,6 +130,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("db") = py::none(), py::arg("dgamma") = py::none(), py::arg("dbeta") = py::none(),
         py::arg("dy2") = py::none(), py::arg("dy1") = py::none());
   m.def("dp_reduce_adamw", &revpp::dp_reduce_adamw);
+  m.def("pointer_info", &revpp::pointer_info);
   m.def("flag_wait_probe", &revpp::flag_wait_probe, py::arg("flag"), py::arg("expect"), py::arg("timeout_s"),
         py::arg("result"));
   m.def("cast_colsum", &revpp::cast_colsum, py::arg("inp"), py::arg("out") = py::none(),

@@ -245,6 +245,18 @@ void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<in
   count_launch();
 }
 
+// (memory type, device ordinal) of a device pointer as the driver sees it: used to check
+// peer mappings before any kernel dereferences them.
+std::vector<int64_t> pointer_info(int64_t ptr) {
+  cudaPointerAttributes attr;
+  const cudaError_t e = cudaPointerGetAttributes(&attr, reinterpret_cast<const void*>(ptr));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return {-1, -1};
+  }
+  return {static_cast<int64_t>(attr.type), static_cast<int64_t>(attr.device)};
+}
+
 // Waits (one thread) until *flag >= expect or the time limit passes; result[0] = 1 or -1.
 void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch::Tensor result) {
   REVPP_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt, "flag must be an int32 CUDA tensor");

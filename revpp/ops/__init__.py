@@ -83,7 +83,11 @@ def attention_fwd(qkv, out, lse, B, S, heads):
 
 
 def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads):
-    ext().attn_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads)
+    """Flash attention backward (tcgen05; REVPP_ATTN_TC=0 selects the mma.sync kernel)."""
+    if _ATTN_TC:
+        ext().attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads)
+    else:
+        ext().attn_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads)
 
 
 __all__ = [

@@ -77,6 +77,12 @@ class FusedP2PReducer:
                     self.ptrs[key].append(ptr)
         if flat.shadow is None:
             self.ptrs["shadow"] = []
+        # every mapped pointer must be device memory before a kernel touches it
+        for key, lst in self.ptrs.items():
+            for d, ptr in enumerate(lst):
+                kind, _ = self.C.pointer_info(int(ptr))
+                if kind != 2:  # cudaMemoryTypeDevice
+                    raise RuntimeError(f"replica {d} {key} mapping is not device memory (type {kind})")
         self.epoch = 0
         self.timeout_s = float(os.environ.get("REVPP_P2P_TIMEOUT_S", "60"))
 

@@ -69,3 +69,30 @@ def test_attn_fwd_tcgen05(B, S, heads):
     assert (out.double() - o_ref).abs().max().item() < 2e-2
     assert (lse.double() - lse_ref).abs().max().item() < 2e-3
     assert (out.double() - out2.double()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3), (1, 1024, 2)])
+def test_attn_bwd_tcgen05(B, S, heads):
+    """tcgen05 backward against float64 autograd and against the mma.sync backward."""
+    C = _C()
+    H = heads * 64
+    qkv = (torch.randn(B * S, 3 * H, device="cuda") * 1.5).to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+    dout = torch.randn(B * S, H, device="cuda").to(torch.bfloat16)
+    dq_acc = torch.empty(B * S, H, device="cuda")
+    D = torch.empty(B, heads, S, device="cuda")
+    dqkv = torch.empty_like(qkv)
+    C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, D, B, S, heads)
+    dqkv2 = torch.empty_like(qkv)
+    C.attn_bwd(qkv, out, dout, lse, dqkv2, dq_acc, D, B, S, heads)
+    torch.cuda.synchronize()
+    assert C.status_read_and_clear() == 0
+    qd = qkv.double().requires_grad_()
+    o_ref, _ = _ref(qd, B, S, heads)
+    o_ref.backward(dout.double())
+    g = qd.grad
+    scale = 1 + g.abs().max().item()
+    assert (dqkv.double() - g).abs().max().item() < 3e-2 * scale
+    assert (dqkv.double() - dqkv2.double()).abs().max().item() < 3e-2 * scale

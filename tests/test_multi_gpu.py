@@ -28,6 +28,11 @@ def _run(mode, n=2, timeout=240):
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_mgpu_worker.py"), mode]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    if p.returncode != 0:
+        out_dir = os.path.join(os.environ.get("GRAFT_REPO_ROOT", os.path.dirname(HERE)), "gpurun_out")
+        if os.path.isdir(out_dir):
+            with open(os.path.join(out_dir, f"mgpu_{mode}_fail.log"), "w") as fh:
+                fh.write(p.stdout + "\n----- stderr -----\n" + p.stderr)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
     res = [json.loads(l[len("RESULT "):]) for l in p.stdout.splitlines() if l.startswith("RESULT ")]
     return sorted(res, key=lambda r: r["rank"])
