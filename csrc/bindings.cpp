@@ -46,6 +46,9 @@ void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<in
                      double timeout_s, bool zero_grad);
 void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch::Tensor result);
 std::vector<int64_t> pointer_info(int64_t ptr);
+int64_t ipc_open(const std::string& handle_bytes);
+void ipc_close(int64_t base);
+std::vector<std::string> ipc_export(const torch::Tensor& t);
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
                  int64_t S, int64_t heads);
@@ -131,6 +134,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dy2") = py::none(), py::arg("dy1") = py::none());
   m.def("dp_reduce_adamw", &revpp::dp_reduce_adamw);
   m.def("pointer_info", &revpp::pointer_info);
+  m.def("ipc_open", [](py::bytes h) { return revpp::ipc_open(std::string(h)); });
+  m.def("ipc_close", &revpp::ipc_close);
+  m.def("ipc_export", [](const torch::Tensor& t) {
+    auto v = revpp::ipc_export(t);
+    return py::make_tuple(py::bytes(v[0]), std::stoll(v[1]));
+  });
   m.def("flag_wait_probe", &revpp::flag_wait_probe, py::arg("flag"), py::arg("expect"), py::arg("timeout_s"),
         py::arg("result"));
   m.def("cast_colsum", &revpp::cast_colsum, py::arg("inp"), py::arg("out") = py::none(),

@@ -22,6 +22,10 @@
 // check that the bounded wait reports an error instead of hanging.
 #include <cooperative_groups.h>
 
+#include <cstring>
+#include <string>
+#include <vector>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(512) dp_reduce_adamw_kernel(DpArgs a) {
 
   // ---- D: barrier 2 (every replica's parameter stores are visible)
   if (blockIdx.x == 0 && threadIdx.x == 0) {
+    __threadfence_system();
     for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 3);
     wait_all_flags(a.flags[a.rank], a.D, base + 3, a.timeout_ns, a.status);
   }
@@ -243,6 +248,63 @@ void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<in
   REVPP_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(dp_reduce_adamw_kernel), dim3(grid), dim3(512),
                                                params, 0, cur_stream()));
   count_launch();
+}
+
+// Map a peer's allocation (CUDA IPC handle bytes) into this process *for the current
+// device*, with lazy peer access; returns the base address.  The mapping must be made
+// with the consuming GPU current: torch's own storage sharing opens handles under the
+// producer's device index, which maps the memory for the wrong GPU in a multi-GPU
+// process group (a kernel on this GPU then faults on the address).
+int64_t ipc_open(const std::string& handle_bytes) {
+  REVPP_CHECK(handle_bytes.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size ", handle_bytes.size());
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle_bytes.data(), sizeof(h));
+  void* p = nullptr;
+  REVPP_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  // the owner GPU must be reachable from the current one: peer access enabled (lazily by
+  // the open above, or already) or the same device
+  int cur = -1;
+  REVPP_CUDA_CHECK(cudaGetDevice(&cur));
+  cudaPointerAttributes attr;
+  REVPP_CUDA_CHECK(cudaPointerGetAttributes(&attr, p));
+  if (attr.device != cur) {
+    int can = 0;
+    REVPP_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, cur, attr.device));
+    if (!can) {
+      cudaIpcCloseMemHandle(p);
+      REVPP_CHECK(false, "GPU ", cur, " cannot access peer GPU ", attr.device);
+    }
+    const cudaError_t e = cudaDeviceEnablePeerAccess(attr.device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();
+    } else if (e != cudaSuccess) {
+      cudaIpcCloseMemHandle(p);
+      REVPP_CHECK(false, "enabling peer access ", cur, " -> ", attr.device, ": ", cudaGetErrorString(e));
+    }
+  }
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t base) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(base)); }
+
+// IPC handle bytes and byte offset of the allocation containing `t`'s data.
+std::vector<std::string> ipc_export(const torch::Tensor& t) {
+  REVPP_CHECK(t.is_cuda(), "IPC export needs a CUDA tensor");
+  c10::cuda::CUDAGuard guard(t.device());
+  void* ptr = t.data_ptr();
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  REVPP_CUDA_CHECK(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+  REVPP_CHECK(q == cudaDriverEntryPointSuccess && fn != nullptr, "cuMemGetAddressRange unavailable");
+  using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  const CUresult r = reinterpret_cast<Fn>(fn)(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  REVPP_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed ", static_cast<int>(r));
+  cudaIpcMemHandle_t h;
+  REVPP_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  const int64_t off = reinterpret_cast<int64_t>(ptr) - static_cast<int64_t>(base);
+  return {std::string(reinterpret_cast<const char*>(&h), sizeof(h)), std::to_string(off)};
 }
 
 // (memory type, device ordinal) of a device pointer as the driver sees it: used to check

@@ -209,6 +209,8 @@ class Trainer:
     def close(self) -> None:
         if self.comms is not None:
             self.comms.drain()
+        if self.dp_reducer is not None and hasattr(self.dp_reducer, "close"):
+            self.dp_reducer.close()
 
 
 @dataclass

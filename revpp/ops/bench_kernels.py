@@ -1,0 +1,172 @@
+"""Per-kernel microbenchmarks of the sm_100a extension (CUDA-event timing).
+
+    python -m revpp.ops.bench_kernels gemm --M 16384 --N 4096 --K 1024 --epi gelu --variant 2
+    python -m revpp.ops.bench_kernels attn-fwd --B 16 --S 512 --heads 16
+    python -m revpp.ops.bench_kernels attn-bwd --B 16 --S 512 --heads 16
+    python -m revpp.ops.bench_kernels layernorm --M 16384 --H 1024
+    python -m revpp.ops.bench_kernels adamw --n 335000000
+
+Each run warms up, then times ``--iters`` launches between CUDA events and prints one JSON
+line with the time per launch and the achieved TFLOP/s or GB/s.  ``--iters 1 --warmup 1``
+gives a short, fixed launch sequence for profiler captures.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+EPIS = {"bf16": 0, "gelu": 1, "resid": 2, "atomic": 3, "dgelu": 4, "f32": 5}
+
+
+def _time(fn, warmup: int, iters: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_gemm(a, C):
+    M, N, K = a.M, a.N, a.K
+    epi = EPIS[a.epi]
+    dev = "cuda"
+    if a.layout == "wgrad":  # C[N_out, K_in] += dY[T, N]^T X[T, K]
+        A = torch.randn(K, M, device=dev).to(torch.bfloat16)
+        B = torch.randn(K, N, device=dev).to(torch.bfloat16)
+        out = torch.zeros(M, N, device=dev)
+        splits = C.gemm_suggest_splits(M, N, K)
+        fn = lambda: C.gemm_tc(A, True, B, True, M, N, K, 3, out, splits=splits, variant=a.variant)  # noqa: E731
+    elif a.layout == "dgrad":
+        A = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        B = (torch.randn(K, N, device=dev) * 0.05).to(torch.bfloat16)
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        aux = torch.randn(M, N, device=dev).to(torch.bfloat16) if epi == 4 else None
+        fn = lambda: C.gemm_tc(A, False, B, True, M, N, K, epi, out, aux=aux, variant=a.variant)  # noqa: E731
+    else:
+        A = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        B = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
+        bias = torch.zeros(N, device=dev, dtype=torch.bfloat16)
+        f32 = epi in (2, 5)
+        out = torch.empty(M, N, device=dev, dtype=torch.float32 if f32 else torch.bfloat16)
+        aux = torch.empty(M, N, device=dev, dtype=torch.bfloat16) if epi == 1 else None
+        resid = torch.randn(M, N, device=dev) if epi == 2 else None
+        fn = lambda: C.gemm_tc(A, False, B, False, M, N, K, epi, out, bias=bias, aux_out=aux,  # noqa: E731
+                               resid=resid, variant=a.variant)
+    ms = _time(fn, a.warmup, a.iters)
+    return {"op": "gemm", "layout": a.layout, "epi": a.epi, "variant": a.variant, "M": M, "N": N, "K": K,
+            "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9}
+
+
+def bench_attn(a, C, backward: bool):
+    B, S, heads = a.B, a.S, a.heads
+    H = heads * 64
+    qkv = torch.randn(B * S, 3 * H, device="cuda").to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    fwd = C.attn_fwd_tc if a.impl == "tc" else C.attn_fwd
+    fwd(qkv, out, lse, B, S, heads)
+    flops = 4.0 * B * S * S * H
+    if not backward:
+        ms = _time(lambda: fwd(qkv, out, lse, B, S, heads), a.warmup, a.iters)
+        return {"op": "attn-fwd", "impl": a.impl, "B": B, "S": S, "heads": heads, "ms": ms,
+                "tflops": flops / ms / 1e9}
+    dout = torch.randn_like(out)
+    dqkv = torch.empty_like(qkv)
+    dq = torch.empty(B * S, H, device="cuda")
+    D = torch.empty(B, heads, S, device="cuda")
+    bwd = C.attn_bwd_tc if a.impl == "tc" else C.attn_bwd
+    ms = _time(lambda: bwd(qkv, out, dout, lse, dqkv, dq, D, B, S, heads), a.warmup, a.iters)
+    return {"op": "attn-bwd", "impl": a.impl, "B": B, "S": S, "heads": heads, "ms": ms,
+            "tflops": 2.5 * flops / ms / 1e9}
+
+
+def bench_layernorm(a, C):
+    M, H = a.M, a.H
+    x = torch.randn(M, H, device="cuda")
+    g = torch.ones(H, device="cuda")
+    b = torch.zeros(H, device="cuda")
+    y = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    mean = torch.empty(M, device="cuda")
+    rstd = torch.empty(M, device="cuda")
+    C.layernorm_fwd(x, g, b, 1e-5, y_bf16=y, mean=mean, rstd=rstd)
+    t_f = _time(lambda: C.layernorm_fwd(x, g, b, 1e-5, y_bf16=y, mean=mean, rstd=rstd), a.warmup, a.iters)
+    dy = torch.randn(M, H, device="cuda").to(torch.bfloat16)
+    resid = torch.randn(M, H, device="cuda")
+    dx = torch.empty(M, H, device="cuda")
+    dxb = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    dg = torch.zeros(H, device="cuda")
+    db = torch.zeros(H, device="cuda")
+    cs = torch.zeros(H, device="cuda")
+    t_b = _time(lambda: C.layernorm_bwd(dy, x, g, mean, rstd, dgamma=dg, dbeta=db, resid=resid, dx_f32=dx,
+                                        dx_bf16=dxb, colsum=cs), a.warmup, a.iters)
+    fwd_bytes = M * H * (4 + 2)
+    bwd_bytes = M * H * (2 + 4 + 4 + 4 + 2)
+    return {"op": "layernorm", "M": M, "H": H, "fwd_ms": t_f, "fwd_gbs": fwd_bytes / t_f / 1e6, "bwd_ms": t_b,
+            "bwd_gbs": bwd_bytes / t_b / 1e6}
+
+
+def bench_adamw(a, C):
+    n = (a.n + 63) // 64 * 64
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(1, device="cuda")
+    step = [0]
+
+    def fn():
+        step[0] += 1
+        ss.zero_()
+        C.grad_sumsq(g, ss)
+        C.adamw_step(p, g, m, v, shadow=sh, lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-6, wd=0.01, step=step[0],
+                     max_norm=1.0, sumsq=ss, zero_grad=False)
+
+    ms = _time(fn, a.warmup, a.iters)
+    bytes_ = n * (4 + 4 * 4 + 4 * 3 + 2)  # norm read + (g, p, m, v) read + (p, m, v) write + shadow
+    return {"op": "adamw", "n": n, "ms": ms, "gbs": bytes_ / ms / 1e6}
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "layernorm", "adamw"])
+    p.add_argument("--M", type=int, default=16384)
+    p.add_argument("--N", type=int, default=4096)
+    p.add_argument("--K", type=int, default=1024)
+    p.add_argument("--H", type=int, default=1024)
+    p.add_argument("--epi", choices=list(EPIS), default="bf16")
+    p.add_argument("--layout", choices=["fwd", "dgrad", "wgrad"], default="fwd")
+    p.add_argument("--variant", type=int, default=0)
+    p.add_argument("--B", type=int, default=16)
+    p.add_argument("--S", type=int, default=512)
+    p.add_argument("--heads", type=int, default=16)
+    p.add_argument("--impl", choices=["tc", "mma"], default="tc")
+    p.add_argument("--n", type=int, default=335_000_000)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--iters", type=int, default=20)
+    a = p.parse_args(argv)
+    from revpp.ops import ext
+
+    C = ext()
+    if a.op == "gemm":
+        r = bench_gemm(a, C)
+    elif a.op == "attn-fwd":
+        r = bench_attn(a, C, False)
+    elif a.op == "attn-bwd":
+        r = bench_attn(a, C, True)
+    elif a.op == "layernorm":
+        r = bench_layernorm(a, C)
+    else:
+        r = bench_adamw(a, C)
+    r["status"] = C.status_read_and_clear()
+    print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

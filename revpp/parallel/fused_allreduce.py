@@ -2,14 +2,13 @@
 
 At construction every replica of a stage exports CUDA IPC handles of its flat fp32
 parameters, fp32 gradients, bf16 shadow weights and a zeroed flag page, gathers the
-peers' handles over the data-parallel process group and maps them.  Each step then runs
-one cooperative kernel per GPU (``revpp._C.dp_reduce_adamw``, csrc/comm.cu): peers' gradient
-shards are read with plain loads, averaged, the clip norm is exchanged through the flag
-pages, AdamW updates this rank's shard and the updated parameters are stored into every
-replica.  All waits in the kernel are bounded and report ``kStatusFlagTimeout``.
-
-torch's CUDA storage sharing (``_share_cuda_`` / ``_new_shared_cuda``) is used only to
-export and open the IPC handles; the data movement is the kernel's.
+peers' handles over the data-parallel process group and maps them *for its own GPU*
+(``revpp._C.ipc_open`` runs cudaIpcOpenMemHandle with this rank's device current and lazy
+peer access).  Each step then runs one cooperative kernel per GPU
+(``revpp._C.dp_reduce_adamw``, csrc/comm.cu): peers' gradient shards are read with plain
+loads, averaged, the clip norm is exchanged through the flag pages, AdamW updates this
+rank's shard and the updated parameters are stored into every replica.  All waits in the
+kernel are bounded and report ``kStatusFlagTimeout``.
 """
 from __future__ import annotations
 
@@ -17,18 +16,6 @@ import os
 
 import torch
 import torch.distributed as dist
-
-
-def _export(t: torch.Tensor):
-    st = t.untyped_storage()
-    meta = st._share_cuda_()
-    elem_off = t.storage_offset() * t.element_size()
-    return meta, elem_off, t.numel(), str(t.dtype)
-
-
-def _open(meta, elem_off):
-    st = torch.UntypedStorage._new_shared_cuda(*meta)
-    return st, st.data_ptr() + elem_off
 
 
 class FusedP2PReducer:
@@ -49,40 +36,31 @@ class FusedP2PReducer:
         if trainer.cfg.global_clip:
             raise RuntimeError("global clipping across stages is not fused; using NCCL")
         dev = flat.device
-        self.flags = torch.zeros(128, dtype=torch.int32, device=dev)
+        self.device = dev
+        # a flag page of its own allocation (128 int32 words, padded to its own segment)
+        self.flags = torch.zeros(1 << 18, dtype=torch.int32, device=dev)[:128]
         self.scratch = torch.zeros(2, dtype=torch.float32, device=dev)
         torch.cuda.synchronize(dev)
-        mine = {
-            "grad": _export(flat.grad),
-            "param": _export(flat.data),
-            "shadow": _export(flat.shadow) if flat.shadow is not None else None,
-            "flags": _export(self.flags),
-            "pid": os.getpid(),
-        }
+        own = {"grad": flat.grad, "param": flat.data, "shadow": flat.shadow, "flags": self.flags}
+        mine = {k: (self.C.ipc_export(t) if t is not None else None) for k, t in own.items()}
         allh = [None] * self.D
         dist.all_gather_object(allh, mine, group=group)
-        self._keep = []  # opened storages stay alive for the mappings' lifetime
+        self._bases = {}  # handle bytes -> mapped base (each peer segment mapped once)
         self.ptrs = {"grad": [], "param": [], "shadow": [], "flags": []}
-        own = {"grad": flat.grad, "param": flat.data, "shadow": flat.shadow, "flags": self.flags}
-        for d, h in enumerate(allh):
-            for key in ("grad", "param", "shadow", "flags"):
-                if key == "shadow" and h["shadow"] is None:
-                    continue
-                if d == self.rank_in_group:
-                    self.ptrs[key].append(own[key].data_ptr())
-                else:
-                    meta, off, _, _ = h[key]
-                    st, ptr = _open(meta, off)
-                    self._keep.append(st)
-                    self.ptrs[key].append(ptr)
+        with torch.cuda.device(dev):
+            for d, h in enumerate(allh):
+                for key in ("grad", "param", "shadow", "flags"):
+                    if own[key] is None:
+                        continue
+                    if d == self.rank_in_group:
+                        self.ptrs[key].append(own[key].data_ptr())
+                        continue
+                    handle, off = h[key]
+                    if handle not in self._bases:
+                        self._bases[handle] = self.C.ipc_open(handle)
+                    self.ptrs[key].append(self._bases[handle] + int(off))
         if flat.shadow is None:
             self.ptrs["shadow"] = []
-        # every mapped pointer must be device memory before a kernel touches it
-        for key, lst in self.ptrs.items():
-            for d, ptr in enumerate(lst):
-                kind, _ = self.C.pointer_info(int(ptr))
-                if kind != 2:  # cudaMemoryTypeDevice
-                    raise RuntimeError(f"replica {d} {key} mapping is not device memory (type {kind})")
         self.epoch = 0
         self.timeout_s = float(os.environ.get("REVPP_P2P_TIMEOUT_S", "60"))
 
@@ -97,3 +75,9 @@ class FusedP2PReducer:
 
     def reduce(self, grad) -> None:  # pragma: no cover - the fused path never splits the update
         raise RuntimeError("FusedP2PReducer updates parameters itself; call reduce_and_update")
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for base in self._bases.values():
+            self.C.ipc_close(base)
+        self._bases.clear()

@@ -34,7 +34,12 @@ def _free_port():
 
 
 def _cfg(extra: str, world: int):
-    args = parse_args(("--preset tiny-bert --num-hidden-layers 4 --par-mode pp --batch-size 16 "
+    if "--model vit" in extra:
+        base = ("--model vit --hidden-size 128 --num-attention-heads 2 --img-size 32 --patch-size 8 "
+                "--num-classes 10 ")
+    else:
+        base = "--preset tiny-bert "
+    args = parse_args((base + "--num-hidden-layers 4 --par-mode pp --batch-size 16 "
                        "--microbatch-size 4 --num-microbatches 4 --device cpu --lr 1e-3 " + extra).split())
     return build_global_config(args)
 
@@ -50,12 +55,14 @@ def _oracle(cfg, P, batch):
     eh0 = TorchEmbedHead(mods[0], flats[0], torch.float32)
     ehl = TorchEmbedHead(mods[-1], flats[-1], torch.float32)
     n = cfg.num_microbatches
-    ids = torch.chunk(batch["input_ids"], n)
-    tt = torch.chunk(batch["attention_mask"], n)
+    if cfg.model == "bert":
+        inputs = list(zip(torch.chunk(batch["input_ids"], n), torch.chunk(batch["attention_mask"], n)))
+    else:
+        inputs = [(x,) for x in torch.chunk(batch["images"], n)]
     labels = torch.chunk(batch["labels"], n)
     total = 0.0
     for i in range(n):
-        x = eh0._embed((ids[i], tt[i]))
+        x = eh0._embed(inputs[i])
         reversible = cfg.reversible
         x2, x1 = x, x
         for s in range(P):
@@ -119,6 +126,7 @@ def _run(extra: str, world: int = 2):
 
 @pytest.mark.parametrize("extra", [
     "--reversible",
+    "--reversible --model vit",
     "--reversible --schedule gpipe",
     "--reversible --is_pareprop",
     "--reversible --inverse",
