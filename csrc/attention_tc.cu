@@ -734,3 +734,131 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
 }
 
 }  // namespace revpp
+
+// ------------------------------------------------------------------ allocation-free entry point
+// Declared (and documented for users) in attention_noalloc.h.  It launches the same four
+// steps as attn_bwd_tc above (zero dQ accumulator, D = rowsum(dO * O), the tcgen05
+// backward kernel, dQ conversion) with its temporaries in the file-scope array below.
+#include <mutex>
+
+#include "attention_noalloc.h"
+
+namespace revpp {
+
+__global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                    float* __restrict__ D, int M, int S, int heads);
+__global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, long long M,
+                                       int H);
+
+namespace {
+
+// [0, 256): fallback status word; then the fp32 dQ accumulator; then D (256-byte aligned)
+static __device__ __align__(256) unsigned char g_attn_bwd_scratch[REVPP_ATTN_BWD_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_scratch_dev[kNoAllocMaxDevices] = {};
+
+int noalloc_fail(int code, char* err, size_t errlen, const std::string& msg) {
+  if (err != nullptr && errlen > 0) {
+    const size_t n = std::min(errlen - 1, msg.size());
+    std::memcpy(err, msg.data(), n);
+    err[n] = '\0';
+  }
+  return code;
+}
+
+// Once per device, with that device current: the scratch array's device address and the
+// backward kernel's dynamic shared-memory limit.
+cudaError_t noalloc_setup(int dev, unsigned char** scratch) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_scratch_dev[dev] == nullptr) {
+    unsigned char* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_attn_bwd_scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::total + 1024);
+    if (e != cudaSuccess) return e;
+    g_noalloc_scratch_dev[dev] = p;
+  }
+  *scratch = g_noalloc_scratch_dev[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace revpp
+
+extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const void* dout, const float* lse,
+                                         void* dqkv, int B, int S, int heads, int* status, void* stream, char* err,
+                                         size_t errlen) {
+  using namespace revpp;
+  if (!qkv || !out || !dout || !lse || !dqkv || B <= 0 || S <= 0 || heads <= 0)
+    return noalloc_fail(REVPP_NOALLOC_BAD_ARGUMENT, err, errlen, "null pointer or non-positive size");
+  for (const void* p : {qkv, out, dout, static_cast<const void*>(lse), static_cast<const void*>(dqkv)})
+    if (reinterpret_cast<uintptr_t>(p) & 15)
+      return noalloc_fail(REVPP_NOALLOC_BAD_ARGUMENT, err, errlen, "every buffer must be 16-byte aligned");
+  const long long H = 64LL * heads;
+  const long long M = static_cast<long long>(B) * S;
+  const unsigned long long dq_bytes = (static_cast<unsigned long long>(M * H) * 4ULL + 255ULL) & ~255ULL;
+  const unsigned long long d_bytes = static_cast<unsigned long long>(M) * heads * 4ULL;
+  const unsigned long long need = 256ULL + dq_bytes + d_bytes;
+  if (need > REVPP_ATTN_BWD_NOALLOC_SCRATCH_BYTES)
+    return noalloc_fail(REVPP_NOALLOC_TOO_LARGE, err, errlen,
+                        "attention backward needs " + std::to_string(need) + " bytes of scratch for B=" +
+                            std::to_string(B) + " S=" + std::to_string(S) + " heads=" + std::to_string(heads) +
+                            "; the allocation-free entry point holds " +
+                            std::to_string(REVPP_ATTN_BWD_NOALLOC_SCRATCH_BYTES) + " bytes");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, "no usable current CUDA device");
+  unsigned char* scratch = nullptr;
+  e = noalloc_setup(dev, &scratch);
+  if (e != cudaSuccess)
+    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("set-up: ") + cudaGetErrorString(e));
+  int* st_word = status ? status : reinterpret_cast<int*>(scratch);
+  float* dq_acc = reinterpret_cast<float*>(scratch + 256);
+  float* Dbuf = reinterpret_cast<float*>(scratch + 256 + dq_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  CUtensorMap tq, tdo;
+  try {
+    const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    tq = make_tmap_2d(qkv, bf, 2, 3 * H, M, 3 * H * 2, 64, 128, sw);
+    tdo = make_tmap_2d(dout, bf, 2, H, M, H * 2, 64, 128, sw);
+  } catch (const std::exception& ex) {
+    return noalloc_fail(REVPP_NOALLOC_BAD_ARGUMENT, err, errlen, ex.what());
+  }
+  e = cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(M * H) * sizeof(float), st);
+  if (e != cudaSuccess)
+    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("memset: ") + cudaGetErrorString(e));
+  {
+    const long long threads = 256;
+    const long long blocks = (M * heads * 32 + threads - 1) / threads;
+    attn_bwd_dot_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, st>>>(
+        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), Dbuf, static_cast<int>(M), S,
+        heads);
+  }
+  AttnBwdTcArgs a;
+  a.lse = lse;
+  a.D = Dbuf;
+  a.dq_acc = dq_acc;
+  a.dqkv = static_cast<__nv_bfloat16*>(dqkv);
+  a.S = S;
+  a.heads = heads;
+  a.scale = static_cast<float>(1.0 / std::sqrt(64.0));
+  a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
+  a.status = st_word;
+  dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, BwdSmem::total + 1024, st>>>(tq, tdo, a);
+  {
+    const long long n4 = M * H / 4;
+    const long long threads = 256;
+    attn_dq_convert_kernel<<<static_cast<unsigned>((n4 + threads - 1) / threads), static_cast<unsigned>(threads), 0,
+                             st>>>(dq_acc, static_cast<__nv_bfloat16*>(dqkv), M, static_cast<int>(H));
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("launch: ") + cudaGetErrorString(e));
+  return REVPP_NOALLOC_OK;
+}
