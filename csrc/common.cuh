@@ -2,7 +2,7 @@
 //
 // Every wait in these kernels is bounded: an mbarrier or flag wait that does
 // not complete within the time limit records an error code in the status word
-// (see status.cu) and returns false, so the kernel can unwind (wait for its own
+// (host.cpp: status_device_ptr) and returns false, so the kernel can unwind (wait for its own
 // copies, free TMEM, return) instead of hanging the GPU.  No kernel here uses
 // __trap() or device asserts.
 #pragma once
