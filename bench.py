@@ -6,6 +6,12 @@ pipeline-parallel over N GPUs (PP = N, 1F1B, one rank per GPU), global batch 512
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N --steps K --warmup W
     ... --impl reference        # the reference implementation on the same config
 
+Secondary workloads (same JSON line; the reference arm covers the headline only):
+    --model {bert-base,vit-b16,vit-l16-384}  --seq S (BERT)  --layers L
+    --dp D          pipeline replicas: PP = N / D, replicas reduced by the fused NVLink kernel
+    --stage {standard,checkpoint}            non-reversible stages for comparison
+    --microbatch-size M --global-batch B     micro-batches per replica = B / (M * D)
+
 Reported (rank 0 prints one JSON line):
   value  - samples/s of the whole job: global_batch / step time, where the step time is
            K full training steps (pipeline forward/backward of every micro-batch, gradient
@@ -49,7 +55,20 @@ def parse():
     p.add_argument("--layers", type=int, default=MODEL["layers"])
     p.add_argument("--pareprop", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    return p.parse_args()
+    p.add_argument("--model", choices=["bert-large", "bert-base", "vit-b16", "vit-l16-384"], default="bert-large",
+                   help="secondary workloads; the headline is bert-large")
+    p.add_argument("--dp", type=int, default=1, help="pipeline replicas: PP = gpus / dp")
+    p.add_argument("--stage", choices=["reversible", "standard", "checkpoint"], default="reversible")
+    a = p.parse_args()
+    if a.model != "bert-large" and a.layers == MODEL["layers"]:
+        a.layers = None  # the preset's depth
+    if a.gpus % a.dp != 0:
+        p.error("--gpus must be a multiple of --dp")
+    return a
+
+
+MODEL_NAMES = {"bert-large": "Rev-BERT-Large", "bert-base": "Rev-BERT-Base", "vit-b16": "Rev-ViT-B/16",
+               "vit-l16-384": "Rev-ViT-L/16@384"}
 
 
 def dist_setup(n_gpus: int):
@@ -90,16 +109,30 @@ def sum_over_ranks(x: float, dev) -> float:
 
 
 def base_record(args, world, impl):
-    nmb = args.global_batch // args.microbatch_size
+    from revpp.config import PRESETS
+
+    pre = PRESETS[args.model]
+    nmb = args.global_batch // (args.microbatch_size * args.dp)
+    P = world // args.dp
+    name = MODEL_NAMES[args.model]
+    if args.stage != "reversible":
+        name = name.replace("Rev-", "") + f" ({args.stage} stages)"
+    if pre["model"] == "bert":
+        seq = args.seq
+        data = "synthetic (uniform token ids, all-ones mask, Bernoulli labels), random init"
+    else:
+        seq = (pre["img_size"] // pre["patch_size"]) ** 2 + 1
+        data = "synthetic (i.i.d. N(0,1) pixels, uniform labels), random init"
+    par = f"pp{P}" + (f"xdp{args.dp}" if args.dp > 1 else "")
     return {
         "metric": METRIC, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (uniform token ids, all-ones mask, Bernoulli labels), random init",
+        "data": data,
         "impl": impl,
-        "config": {"model": "Rev-BERT-Large", "layers": args.layers, "hidden": MODEL["hidden"],
-                   "heads": MODEL["heads"], "global_batch": args.global_batch, "seq_len": args.seq,
+        "config": {"model": name, "layers": args.layers or pre["num_hidden_layers"], "hidden": pre["hidden_size"],
+                   "heads": pre["num_attention_heads"], "global_batch": args.global_batch, "seq_len": seq,
                    "microbatch_size": args.microbatch_size, "num_microbatches": nmb,
-                   "parallelism": f"pp{world}", "schedule": "1f1b",
+                   "parallelism": par, "schedule": "1f1b",
                    "backward": "pareprop" if args.pareprop else "sequential",
                    "l2": "no flush: per-step working set (weights, Adam state, activations) >> 126 MB L2"},
     }
@@ -118,20 +151,29 @@ def run_revpp(args):
     from revpp.utils.logger import build_logger
     from revpp.utils.seed import set_seed
 
+    from revpp.config import PRESETS
+
     C = ext()
-    nmb = args.global_batch // args.microbatch_size
-    cfg = GlobalConfig(model="bert", par_mode=ParMode.PP if world > 1 else ParMode.NONE, reversible=True,
-                       is_pareprop=args.pareprop, num_hidden_layers=args.layers, hidden_size=MODEL["hidden"],
-                       num_attention_heads=MODEL["heads"], max_position_embeddings=args.seq, num_classes=2,
+    P = world // args.dp
+    nmb = args.global_batch // (args.microbatch_size * args.dp)  # per replica
+    pre = dict(PRESETS[args.model])
+    if args.layers:
+        pre["num_hidden_layers"] = args.layers
+    if pre["model"] == "bert":
+        pre["max_position_embeddings"] = args.seq
+    par_mode = ParMode.PP if P > 1 or args.dp > 1 else ParMode.NONE
+    cfg = GlobalConfig(par_mode=par_mode, reversible=args.stage == "reversible",
+                       checkpointing=args.stage == "checkpoint", is_pareprop=args.pareprop, dp=args.dp,
                        autocast_dtype=torch.bfloat16, batch_size=args.global_batch,
-                       microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-5, dataset="synthetic")
+                       microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-5, dataset="synthetic",
+                       **pre)
     lg = build_logger(f"bench{rank}", None)
     env = EnvContext(world_size=world, rank=rank, local_rank=local, device=dev, proc_logger=lg, node_logger=None,
                      main_logger=None, pg=dist.group.WORLD if dist.is_initialized() else None,
-                     master_rank=world - 1, num_stages=world, replicas=1)
+                     master_rank=world - 1, num_stages=P, replicas=args.dp)
     set_seed(cfg.seed + rank)
     tr = Trainer(cfg, env)
-    data = SyntheticBatches(cfg, args.global_batch, 4, seed=0)
+    data = SyntheticBatches(cfg, tr.local_batch, 4, seed=tr.replica)
     batches = [data.make(i) for i in range(4)] if tr.is_first else [None] * 4
 
     for i in range(args.warmup):
@@ -191,7 +233,7 @@ def run_revpp(args):
     # the loss lives on the last rank; rank 0 prints
     if dist.is_initialized():
         obj = [rec.get("final_loss")]
-        dist.broadcast_object_list(obj, src=world - 1)
+        dist.broadcast_object_list(obj, src=P - 1)
         rec["final_loss"] = obj[0]
     if rank == 0:
         print(json.dumps(rec), flush=True)
@@ -207,6 +249,11 @@ REF_ROOT = os.path.join(HERE, "baseline", "_ref", "BERT")
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.model != "bert-large" or args.dp != 1 or args.stage != "reversible":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm runs the headline workload "
+                              "(reversible BERT-Large, pure PP) only"}), flush=True)
+        return
     if not os.path.isdir(REF_ROOT):
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)

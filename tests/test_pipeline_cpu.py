@@ -89,12 +89,19 @@ def _worker(rank, world, port, extra, q):
         env = build_env(cfg, timeout_s=120)
         set_seed(cfg.seed + rank)
         tr = Trainer(cfg, env)
-        batch = SyntheticBatches(cfg, cfg.batch_size, 1, seed=123).make(0)
+        # each pipeline replica reads its own local batch
+        batch = SyntheticBatches(cfg, tr.local_batch, 1, seed=123 + tr.replica).make(0)
         inputs = tr.split_inputs(batch) if tr.is_first else None
         labels = batch["labels"] if tr.is_first else None
         losses = tr.executor.step(inputs, labels, train=True)
+        if tr.dp_reducer is not None:
+            tr.dp_reducer.reduce(tr.flat.grad)
         grads = {name: g.clone() for name, g in tr.flat.named_grads()}
         loss = float(torch.stack(losses).mean()) if tr.is_last else None
+        if tr.dp_reducer is not None:
+            # the optimizer step must leave every replica with the same parameters
+            tr.opt.step(tr.opt.grad_sumsq())
+            grads["__params__"] = tr.flat.data.clone()
         gathered = [None] * world
         dist.all_gather_object(gathered, (loss, grads))
         tr.close()
@@ -161,3 +168,26 @@ def test_four_stage_reversible():
         for name, g in gathered[s][1].items():
             r = ref_grads[s][name]
             assert (g - r).abs().max().item() <= 1e-5 * max(r.abs().max().item(), 1e-3), (s, name)
+
+
+def test_pipeline_replicas_average_gradients():
+    """PP = 2 x DP = 2 on 4 gloo ranks: after the replica all-reduce every stage holds the
+    mean of the two replicas' gradients (each replica on its own local batch), and the
+    optimizer step leaves both replicas with identical parameters."""
+    extra = "--reversible --dp 2"
+    world = 4
+    gathered = _run(extra, world)
+    cfg = _cfg(extra, world)
+    P = 2
+    local = cfg.batch_size // 2
+    refs = [_oracle(cfg, P, SyntheticBatches(cfg, local, 1, seed=123 + d).make(0)) for d in range(2)]
+    for d in range(2):
+        assert abs(gathered[d * P + P - 1][0] - refs[d][0]) <= 1e-5 * max(1.0, abs(refs[d][0]))
+    for s in range(P):
+        g0, g1 = gathered[s][1], gathered[P + s][1]
+        assert torch.equal(g0.pop("__params__"), g1.pop("__params__")), f"stage {s}: replicas diverged"
+        for name, g in g0.items():
+            r = 0.5 * (refs[0][1][s][name] + refs[1][1][s][name])
+            scale = r.abs().max().item()
+            assert (g - r).abs().max().item() <= 1e-5 * max(scale, 1e-3), (s, name)
+            assert torch.equal(g, g1[name]), (s, name)
