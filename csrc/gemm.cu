@@ -11,7 +11,8 @@
 // Warp roles (320 threads):
 //   warp 0      : TMA producer (one thread), STAGES-deep smem ring, no multicast
 //   warp 1      : TMEM allocator + MMA issuer (one thread), tcgen05.mma 128xBNx16
-//   warps 2..9  : epilogue; TMEM -> registers (tcgen05.ld) -> fused op -> global
+//   warps 2..9  : epilogue; TMEM -> registers (tcgen05.ld) -> fused op -> per-warp smem
+//                 staging tile -> row-contiguous global stores
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of
 // tile i overlaps the main loop of tile i+1.
 //
@@ -52,88 +53,192 @@ constexpr int kGemmBK = 64;
 constexpr int kGemmEpiWarps = 8;
 constexpr int kGemmThreads = 64 + kGemmEpiWarps * 32;
 
-template <int EPI>
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&r)[32]) {
-  if (row >= a.M || col0 >= a.N) return;
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+// ------------------------------------------------------------------ epilogue
+// Each epilogue warp owns 32 TMEM lanes (= 32 output rows) and a run of columns.  A
+// tcgen05.ld gives every thread one row, so writing straight to global memory would make
+// each warp-wide access touch 32 different rows.  Instead every round goes through a
+// 4 KB per-warp staging tile (32 rows x 128 bytes, 16-byte units XOR-swizzled by row, which
+// keeps both access patterns at the 4-wavefront minimum): threads write their row, then
+// the warp moves 4 rows x 128 contiguous bytes per instruction, reading the residual /
+// pre-activation inputs with the same row-contiguous pattern.
+constexpr uint32_t kEpiStageBytes = 32 * 128;
 
-  if constexpr (EPI == kEpiAtomicF32) {
-    float* c = reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0;
+__device__ __forceinline__ uint32_t epi_stg_off(int row, int unit) {
+  return static_cast<uint32_t>(row * 128 + ((unit ^ (row & 7)) << 4));
+}
+
+template <int EPI>
+struct EpiTraits {
+  static constexpr bool kBf16Stage = (EPI == kEpiBF16 || EPI == kEpiGelu || EPI == kEpiDGelu);
+  static constexpr int kCols = kBf16Stage ? 64 : 32;  // output columns per staged round
+  static constexpr int kElemPerUnit = kBf16Stage ? 8 : 4;
+};
+
+// Phase 1: this thread's row of the round into the staging tile.
+template <bool BF16>
+__device__ __forceinline__ void epi_stage_row(uint8_t* stg, int lane, const float* v) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      atomicAdd(reinterpret_cast<float4*>(c + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+  for (int u = 0; u < 8; ++u) {
+    uint4 w;
+    if constexpr (BF16) {
+      w = make_uint4(pack_bf16x2(v[8 * u + 0], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                     pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+    } else {
+      w = make_uint4(__float_as_uint(v[4 * u + 0]), __float_as_uint(v[4 * u + 1]), __float_as_uint(v[4 * u + 2]),
+                     __float_as_uint(v[4 * u + 3]));
     }
-    return;
-  } else {
-    if (a.bias != nullptr && EPI != kEpiDGelu) {
-      const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
+    *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, u)) = w;
+  }
+}
+
+// Phase 2 for a plain copy of the staged tile to a row-major output (bf16 or fp32).
+template <int ELEM_BYTES>
+__device__ __forceinline__ void epi_copy_out(const uint8_t* stg, int lane, void* out, long long ld, int row0, int col0,
+                                             int M, int N) {
+  constexpr int E = 16 / ELEM_BYTES;
+  const int u = lane & 7;
+  const int col = col0 + u * E;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 b = __ldg(bp + j);
-        const float2 b0 = unpack_bf16x2(b.x), b1 = unpack_bf16x2(b.y), b2 = unpack_bf16x2(b.z),
-                     b3 = unpack_bf16x2(b.w);
-        v[8 * j + 0] += b0.x; v[8 * j + 1] += b0.y; v[8 * j + 2] += b1.x; v[8 * j + 3] += b1.y;
-        v[8 * j + 4] += b2.x; v[8 * j + 5] += b2.y; v[8 * j + 6] += b3.x; v[8 * j + 7] += b3.y;
-      }
-    }
-    if constexpr (EPI == kEpiBF16) {
-      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
+  for (int i = 0; i < 8; ++i) {
+    const int rr = 4 * i + (lane >> 3);
+    const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
+    if (row0 + rr < M && col < N)
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + ((static_cast<long long>(row0 + rr) * ld + col) * ELEM_BYTES)) = w;
+  }
+}
+
+// One staged round: `r` holds kCols accumulator columns of this thread's row
+// (row0 + lane), starting at output column col0.
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* stg, int lane, int row0, int col0,
+                                                    const uint32_t* r) {
+  using T = EpiTraits<EPI>;
+  constexpr int NC = T::kCols;
+  float v[NC];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        c[j] = make_uint4(pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                          pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
-      }
-    } else if constexpr (EPI == kEpiGelu) {
-      float h[32];
+  for (int j = 0; j < NC; ++j) v[j] = __uint_as_float(r[j]);
+  if constexpr (EPI != kEpiDGelu && EPI != kEpiAtomicF32) {
+    if (a.bias != nullptr) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        v[j] = bf16r(v[j]);
-        h[j] = gelu_erf(v[j]);
-      }
-      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        c[j] = make_uint4(pack_bf16x2(h[8 * j + 0], h[8 * j + 1]), pack_bf16x2(h[8 * j + 2], h[8 * j + 3]),
-                          pack_bf16x2(h[8 * j + 4], h[8 * j + 5]), pack_bf16x2(h[8 * j + 6], h[8 * j + 7]));
-      }
-      if (a.aux_out != nullptr) {
-        uint4* u = reinterpret_cast<uint4*>(a.aux_out + static_cast<long long>(row) * a.ld_aux + col0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          u[j] = make_uint4(pack_bf16x2(v[8 * j + 0], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+      for (int j = 0; j < NC / 8; ++j) {
+        if (col0 + 8 * j < a.N) {
+          const uint4 b = __ldg(reinterpret_cast<const uint4*>(a.bias + col0) + j);
+          const float2 b0 = unpack_bf16x2(b.x), b1 = unpack_bf16x2(b.y), b2 = unpack_bf16x2(b.z),
+                       b3 = unpack_bf16x2(b.w);
+          v[8 * j + 0] += b0.x; v[8 * j + 1] += b0.y; v[8 * j + 2] += b1.x; v[8 * j + 3] += b1.y;
+          v[8 * j + 4] += b2.x; v[8 * j + 5] += b2.y; v[8 * j + 6] += b3.x; v[8 * j + 7] += b3.y;
         }
       }
-    } else if constexpr (EPI == kEpiResid) {
-      const float4* rs = reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row) * a.ld_resid + col0);
-      float4* c = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
-      const float s = a.sign;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 x = rs[j];
-        c[j] = make_float4(x.x + s * bf16r(v[4 * j + 0]), x.y + s * bf16r(v[4 * j + 1]), x.z + s * bf16r(v[4 * j + 2]),
-                           x.w + s * bf16r(v[4 * j + 3]));
-      }
-    } else if constexpr (EPI == kEpiDGelu) {
-      const uint4* up = reinterpret_cast<const uint4*>(a.aux + static_cast<long long>(row) * a.ld_aux + col0);
-      uint4* c = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 u = up[j];
-        const float2 u0 = unpack_bf16x2(u.x), u1 = unpack_bf16x2(u.y), u2 = unpack_bf16x2(u.z), u3 = unpack_bf16x2(u.w);
-        const float g0 = bf16r(v[8 * j + 0]) * gelu_erf_grad(u0.x), g1 = bf16r(v[8 * j + 1]) * gelu_erf_grad(u0.y);
-        const float g2 = bf16r(v[8 * j + 2]) * gelu_erf_grad(u1.x), g3 = bf16r(v[8 * j + 3]) * gelu_erf_grad(u1.y);
-        const float g4 = bf16r(v[8 * j + 4]) * gelu_erf_grad(u2.x), g5 = bf16r(v[8 * j + 5]) * gelu_erf_grad(u2.y);
-        const float g6 = bf16r(v[8 * j + 6]) * gelu_erf_grad(u3.x), g7 = bf16r(v[8 * j + 7]) * gelu_erf_grad(u3.y);
-        c[j] = make_uint4(pack_bf16x2(g0, g1), pack_bf16x2(g2, g3), pack_bf16x2(g4, g5), pack_bf16x2(g6, g7));
-      }
-    } else if constexpr (EPI == kEpiF32) {
-      float4* c = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.C) + static_cast<long long>(row) * a.ldc + col0);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) c[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
+  }
+  const int u = lane & 7;
+  const int col = col0 + u * T::kElemPerUnit;
+  if constexpr (EPI == kEpiBF16 || EPI == kEpiF32) {
+    epi_stage_row<T::kBf16Stage>(stg, lane, v);
+    __syncwarp();
+    epi_copy_out<T::kBf16Stage ? 2 : 4>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
+  } else if constexpr (EPI == kEpiGelu) {
+    float h[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      v[j] = bf16r(v[j]);
+      h[j] = gelu_erf(v[j]);
+    }
+    epi_stage_row<true>(stg, lane, h);
+    __syncwarp();
+    epi_copy_out<2>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
+    if (a.aux_out != nullptr) {
+      __syncwarp();
+      epi_stage_row<true>(stg, lane, v);
+      __syncwarp();
+      epi_copy_out<2>(stg, lane, a.aux_out, a.ld_aux, row0, col0, a.M, a.N);
+    }
+  } else if constexpr (EPI == kEpiResid) {
+    // C = resid + sign * bf16(acc + bias); the residual is read row-contiguously
+    float4 x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      x[i] = (row0 + rr < a.M && col < a.N)
+                 ? *reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row0 + rr) * a.ld_resid + col)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < NC; ++j) v[j] = bf16r(v[j]);
+    epi_stage_row<false>(stg, lane, v);
+    __syncwarp();
+    const float sg = a.sign;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
+      if (row0 + rr < a.M && col < a.N) {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
+            make_float4(x[i].x + sg * __uint_as_float(w.x), x[i].y + sg * __uint_as_float(w.y),
+                        x[i].z + sg * __uint_as_float(w.z), x[i].w + sg * __uint_as_float(w.w));
+      }
+    }
+  } else if constexpr (EPI == kEpiDGelu) {
+    // C = bf16(bf16(acc) * gelu'(aux)), aux = pre-activation, read row-contiguously
+    uint4 ua[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      ua[i] = (row0 + rr < a.M && col < a.N)
+                  ? *reinterpret_cast<const uint4*>(a.aux + static_cast<long long>(row0 + rr) * a.ld_aux + col)
+                  : make_uint4(0u, 0u, 0u, 0u);
+    }
+    epi_stage_row<true>(stg, lane, v);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
+      if (row0 + rr < a.M && col < a.N) {
+        const uint32_t wa[4] = {w.x, w.y, w.z, w.w};
+        const uint32_t xa[4] = {ua[i].x, ua[i].y, ua[i].z, ua[i].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 g = unpack_bf16x2(wa[e]);
+          const float2 pre = unpack_bf16x2(xa[e]);
+          o[e] = pack_bf16x2(g.x * gelu_erf_grad(pre.x), g.y * gelu_erf_grad(pre.y));
+        }
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  } else if constexpr (EPI == kEpiAtomicF32) {
+    epi_stage_row<false>(stg, lane, v);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
+      if (row0 + rr < a.M && col < a.N) {
+        atomicAdd(reinterpret_cast<float4*>(static_cast<float*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col),
+                  make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w)));
+      }
+    }
+  }
+  __syncwarp();  // the staging tile is rewritten by the next round
+}
+
+// The epilogue of one warp for one tile: HALF_COLS accumulator columns starting at TMEM
+// address `taddr` (lane quarter and column already applied), output rows row0..row0+31,
+// output columns from col0.
+template <int EPI, int HALF_COLS>
+__device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
+                                                   int row0, int col0) {
+  constexpr int RC = EpiTraits<EPI>::kCols;
+#pragma unroll 1
+  for (int c = 0; c < HALF_COLS; c += RC) {
+    if (col0 + c >= a.N) break;  // warp-uniform
+    uint32_t r[RC];
+    tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    if constexpr (RC == 64) tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    tmem_wait_ld();
+    gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r);
   }
 }
 
@@ -155,7 +260,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // kGemmEpiWarps x 4 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kGemmEpiWarps * kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -311,15 +417,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int tn = (t / args.tiles_m) % args.tiles_n;
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
-      const int row = tm * BM + q * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        const int ccol = half * (BN / 2) + c * 32;
-        uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + ccol), r);
-        tmem_wait_ld();
-        gemm_epilogue_chunk<EPI>(args, row, tn * BN + ccol, r);
-      }
+      gemm_epilogue_warp<EPI, BN / 2>(
+          args, sEpi + ew * kEpiStageBytes, lane,
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2)),
+          tm * BM + q * 32, tn * BN + half * (BN / 2));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -367,7 +468,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // kGemmEpiWarps x 4 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kGemmEpiWarps * kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -539,15 +641,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int tn = (t / args.tiles_m) % args.tiles_n;
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
-      const int row = tm * 2 * BM + crank * BM + q * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        const int ccol = half * (BN / 2) + c * 32;
-        uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + ccol), r);
-        tmem_wait_ld();
-        gemm_epilogue_chunk<EPI>(args, row, tn * BN + ccol, r);
-      }
+      gemm_epilogue_warp<EPI, BN / 2>(
+          args, sEpi + ew * kEpiStageBytes, lane,
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2)),
+          tm * 2 * BM + crank * BM + q * 32, tn * BN + half * (BN / 2));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
@@ -574,7 +671,7 @@ namespace {
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                       cudaStream_t st) {
-  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024 + 256;
+  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + kGemmEpiWarps * kEpiStageBytes + 1024 + 256;
   auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   static int configured_for = -1;
   int dev = 0;
@@ -590,7 +687,7 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
 template <int STAGES, bool A_MN, bool B_MN, int EPI>
 void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                        cudaStream_t st) {
-  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + 128 * kGemmBK * 2) + 1024 + 256;
+  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + 128 * kGemmBK * 2) + kGemmEpiWarps * kEpiStageBytes + 1024 + 256;
   auto kern = gemm_tc2_kernel<STAGES, A_MN, B_MN, EPI>;
   static int configured_for = -1;
   int dev = 0;
