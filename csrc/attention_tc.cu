@@ -358,6 +358,10 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 //                        tile)                               -> TMEM cols [384, 448)
 //   dQ warps (one thread per query) add dQ_j * scale into an fp32 buffer with atomics.
 // Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax / final dK dV, 6-9 dQ.
+// Overlap: as soon as the softmax of tile j has consumed S^T / dP^T, the issuer starts
+// S^T / dP^T of tile j+1 and only then the dV / dK / dQ MMAs of tile j, so the softmax of
+// tile j+1 runs while the tensor core works on tile j.  P^T and dS^T are therefore
+// double-buffered in shared memory; LSE and D rows are fetched one tile ahead.
 namespace {
 constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
@@ -367,21 +371,19 @@ constexpr uint32_t kSqTile = 2 * kTile;        // 32 KB: a [128 x 128] bf16 tile
 struct BwdSmem {
   static constexpr uint32_t k = 0;
   static constexpr uint32_t v = k + kTile;
-  static constexpr uint32_t q = v + kTile;          // 2 buffers
-  static constexpr uint32_t dout = q + 2 * kTile;   // 2 buffers
-  static constexpr uint32_t pt = dout + 2 * kTile;  // P^T
-  static constexpr uint32_t dst = pt + kSqTile;     // dS^T
-  static constexpr uint32_t stats = dst + kSqTile;  // lse*log2e [2][128], D [2][128]
-  static constexpr uint32_t bars = stats + 4 * 128 * 4;
+  static constexpr uint32_t q = v + kTile;              // 2 buffers
+  static constexpr uint32_t dout = q + 2 * kTile;       // 2 buffers
+  static constexpr uint32_t pt = dout + 2 * kTile;      // P^T, 2 buffers
+  static constexpr uint32_t dst = pt + 2 * kSqTile;     // dS^T, 2 buffers
+  static constexpr uint32_t stats = dst + 2 * kSqTile;  // lse*log2e [128], D [128]
+  static constexpr uint32_t bars = stats + 2 * 128 * 4;
   static constexpr uint32_t total = bars + 256;
 };
+static_assert(BwdSmem::total + 1024 <= 232448, "attention backward exceeds the shared-memory limit");
 constexpr uint32_t kIdescSq = idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescKD = idesc_bf16(128, 64, false, true);
 constexpr uint32_t kIdescQD = idesc_bf16(128, 64, true, true);
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 }  // namespace
 
 struct AttnBwdTcArgs {
@@ -405,17 +407,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* q_full = bar + 1;     // [2]
   uint64_t* q_empty = bar + 3;    // [2]
   uint64_t* s_full = bar + 5;
-  uint64_t* s_empty = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* p_empty = bar + 8;
+  uint64_t* p_full = bar + 6;
+  uint64_t* p_empty = bar + 7;    // [2] (P^T / dS^T buffers)
   uint64_t* dq_full = bar + 9;
   uint64_t* dq_empty = bar + 10;
   uint64_t* kv_done = bar + 11;
   uint64_t* drain = bar + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  uint64_t* grp_bar = bar + 13;   // the four softmax warps' own barrier (bounded waits)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [2][128]
-  float* s_D = s_lse + 2 * 128;                                        // [2][128]
+  float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [128]
+  float* s_D = s_lse + 128;                                            // [128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -434,13 +436,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 4);
     mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
+    mbar_init(&p_empty[0], 1);
+    mbar_init(&p_empty[1], 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(kv_done, 1);
     mbar_init(drain, 1);
+    mbar_init(grp_bar, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -495,15 +498,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t a_do = smem_u32(smem + BwdSmem::dout);
       const uint32_t a_pt = smem_u32(smem + BwdSmem::pt);
       const uint32_t a_ds = smem_u32(smem + BwdSmem::dst);
-      bool ok = mbar_wait(kv_full, 0, args.status, abort_flag);
-      for (int j = 0; ok && j < nq; ++j) {
+      // S^T_j = K Q_j^T and dP^T_j = V dO_j^T into TMEM [0, 256)
+      auto issue_s = [&](int j) {
         const int bb = j & 1;
-        const uint32_t par = (j >> 1) & 1;
-        const uint32_t jp = j & 1;
-        if (!mbar_wait(&q_full[bb], par, args.status, abort_flag)) break;
-        if (!mbar_wait(s_empty, jp ^ 1u, args.status, abort_flag)) break;
-        tc_fence_after();
-        // S^T = K Q^T ; dP^T = V dO^T
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           umma_bf16_ss(tmem, sdesc_sw128(a_k + k * 32, 16, 1024), sdesc_sw128(a_q + bb * kTile + k * 32, 16, 1024),
@@ -515,28 +512,48 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        sdesc_sw128(a_do + bb * kTile + k * 32, 16, 1024), kIdescSq, k > 0);
         }
         umma_commit(s_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, args.status, abort_flag) && mbar_wait(&q_full[0], 0, args.status, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nq; ++j) {
+        const int bb = j & 1;
+        const uint32_t jp = j & 1;
+        const uint32_t pb = j & 1;
+        // softmax of tile j is done: S/dP TMEM is free, P^T / dS^T of tile j are in buffer pb
         if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
+        tc_fence_after();
+        if (j + 1 < nq) {
+          // start tile j+1 now so its softmax overlaps this tile's gradient MMAs
+          if (!mbar_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status, abort_flag)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
         if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
         tc_fence_after();
+        const uint32_t a_ptj = a_pt + pb * kSqTile;
+        const uint32_t a_dsj = a_ds + pb * kSqTile;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ka = (k >> 2) * kTile + (k & 3) * 32;   // K-major over queries (2 chunks)
           // dV += P^T dO   (B = dO, MN-major: d contiguous, queries as K rows)
-          umma_bf16_ss(tmem + 256, sdesc_sw128(a_pt + ka, 16, 1024),
+          umma_bf16_ss(tmem + 256, sdesc_sw128(a_ptj + ka, 16, 1024),
                        sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
           // dK += dS^T Q
-          umma_bf16_ss(tmem + 320, sdesc_sw128(a_ds + ka, 16, 1024),
+          umma_bf16_ss(tmem + 320, sdesc_sw128(a_dsj + ka, 16, 1024),
                        sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           // dQ = dS K : A = dS (queries contiguous in the dS^T tile -> MN-major, 64-query
           // chunks 16 KB apart), B = K (MN-major: d contiguous, keys as K rows)
-          umma_bf16_ss(tmem + 384, sdesc_sw128(a_ds + k * 2048, kTile, 1024), sdesc_sw128(a_k + k * 2048, 8192, 1024),
+          umma_bf16_ss(tmem + 384, sdesc_sw128(a_dsj + k * 2048, kTile, 1024), sdesc_sw128(a_k + k * 2048, 8192, 1024),
                        kIdescQD, k > 0);
         }
         umma_commit(dq_full);
-        umma_commit(p_empty);
+        umma_commit(&p_empty[pb]);
         umma_commit(&q_empty[bb]);
       }
       umma_commit(kv_done);
@@ -556,25 +573,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* pt_base = smem + BwdSmem::pt;
     uint8_t* ds_base = smem + BwdSmem::dst;
     bool ok = true;
+    uint32_t grp_phase = 0;
+    auto group_sync = [&]() -> bool {  // the four softmax warps, bounded
+      __syncwarp();
+      if (lane == 0) mbar_arrive(grp_bar);
+      const bool w = mbar_wait(grp_bar, grp_phase, args.status, abort_flag);
+      grp_phase ^= 1u;
+      return w;
+    };
+    // LSE / D of the next query tile are fetched one tile ahead
+    float pre_lse = tid < S ? g_lse[tid] * ln2inv : 0.f;
+    float pre_D = tid < S ? g_D[tid] : 0.f;
     for (int j = 0; j < nq; ++j) {
-      const int bb = j & 1;
       const uint32_t jp = j & 1;
-      const int qi = j * kBQ + tid;
-      s_lse[bb * 128 + tid] = qi < S ? g_lse[qi] * ln2inv : 0.f;
-      s_D[bb * 128 + tid] = qi < S ? g_D[qi] : 0.f;
-      named_bar_sync(1, 128);
+      const uint32_t pb = j & 1;
+      if (!group_sync()) {  // every softmax warp is done with the previous tile's stats
+        ok = false;
+        break;
+      }
+      s_lse[tid] = pre_lse;
+      s_D[tid] = pre_D;
+      {
+        const int qn = (j + 1) * kBQ + tid;
+        pre_lse = (j + 1 < nq && qn < S) ? g_lse[qn] * ln2inv : 0.f;
+        pre_D = (j + 1 < nq && qn < S) ? g_D[qn] : 0.f;
+      }
+      if (!group_sync()) {
+        ok = false;
+        break;
+      }
       if (!mbar_wait(s_full, jp, args.status, abort_flag)) {
         ok = false;
         break;
       }
-      if (!mbar_wait(p_empty, jp ^ 1u, args.status, abort_flag)) {
+      if (!mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int sw = r & 7;
-      uint8_t* prow = pt_base + (r >> 3) * 1024 + sw * 128;
-      uint8_t* drow = ds_base + (r >> 3) * 1024 + sw * 128;
+      uint8_t* prow = pt_base + pb * kSqTile + (r >> 3) * 1024 + sw * 128;
+      uint8_t* drow = ds_base + pb * kSqTile + (r >> 3) * 1024 + sw * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t sv[32], dp[32];
@@ -587,12 +626,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int ql0 = c * 32 + e;
           const bool v0 = key_ok && (j * kBQ + ql0 < S);
           const bool v1 = key_ok && (j * kBQ + ql0 + 1 < S);
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[e]) * args.scale_log2 - s_lse[bb * 128 + ql0]) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[e + 1]) * args.scale_log2 - s_lse[bb * 128 + ql0 + 1]) : 0.f;
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[e]) * args.scale_log2 - s_lse[ql0]) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[e + 1]) * args.scale_log2 - s_lse[ql0 + 1]) : 0.f;
           const uint32_t pp = pack_bf16x2(p0, p1);
           const float2 pr = unpack_bf16x2(pp);
-          const float d0 = pr.x * (__uint_as_float(dp[e]) - s_D[bb * 128 + ql0]);
-          const float d1 = pr.y * (__uint_as_float(dp[e + 1]) - s_D[bb * 128 + ql0 + 1]);
+          const float d0 = pr.x * (__uint_as_float(dp[e]) - s_D[ql0]);
+          const float d1 = pr.y * (__uint_as_float(dp[e + 1]) - s_D[ql0 + 1]);
           pw[e >> 1] = pp;
           dw[e >> 1] = pack_bf16x2(d0, d1);
         }
@@ -609,10 +648,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(p_full);
-        mbar_arrive(s_empty);
-      }
+      if (lane == 0) mbar_arrive(p_full);
     }
     // final dK, dV for this warp's keys
     if (ok && mbar_wait(kv_done, 0, args.status, abort_flag)) {

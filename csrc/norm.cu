@@ -68,32 +68,40 @@ __global__ void __launch_bounds__(kLnWarps * 32)
   }
 }
 
+// One warp per row.  The per-column sums (dgamma, dbeta, column sum of dx) accumulate in
+// a per-warp shared-memory slice (each lane owns its columns, so no atomics) instead of
+// 3 x 4 x VPL registers per lane: that keeps the kernel at about 128 registers, two
+// blocks (16 warps) per SM, and lets every lane issue its row's dy / x / residual loads
+// together.  The slices are summed per block at the end, one global atomic per column.
 template <int VPL, bool DY_BF16>
-__global__ void __launch_bounds__(kLnWarps * 32)
+__global__ void __launch_bounds__(kLnWarps * 32, VPL <= 8 ? 2 : 1)
     ln_bwd_kernel(const void* __restrict__ dy_, long long lddy, const float* __restrict__ x, long long ldx,
                   const float* __restrict__ gamma, const float* __restrict__ mean_in,
                   const float* __restrict__ rstd_in, int M, float* __restrict__ dgamma, float* __restrict__ dbeta,
                   const float* __restrict__ resid, long long ldr, float* __restrict__ dx_f32,
                   __nv_bfloat16* __restrict__ dx_bf16, long long lddx, float* __restrict__ colsum) {
   constexpr int H = VPL * 128;
-  __shared__ float s_red[3][H];  // dgamma, dbeta, colsum partials of this block
-  for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) (&s_red[0][0])[i] = 0.f;
-  __syncthreads();
+  extern __shared__ float4 s_acc4[];  // [kLnWarps][3][H / 4]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  float4 acc_g[VPL], acc_b[VPL], acc_c[VPL];
+  const bool want_gb = dgamma != nullptr || dbeta != nullptr;
+  const bool want_cs = colsum != nullptr;
+  float4* acc_g = s_acc4 + (warp * 3 + 0) * (H / 4);
+  float4* acc_b = s_acc4 + (warp * 3 + 1) * (H / 4);
+  float4* acc_c = s_acc4 + (warp * 3 + 2) * (H / 4);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    acc_g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    acc_b[i] = acc_g[i];
-    acc_c[i] = acc_g[i];
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    acc_g[lane + 32 * i] = z;
+    acc_b[lane + 32 * i] = z;
+    acc_c[lane + 32 * i] = z;
   }
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   for (int row = blockIdx.x * kLnWarps + warp; row < M; row += gridDim.x * kLnWarps) {
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * ldx);
+    const float4* rr = resid ? reinterpret_cast<const float4*>(resid + static_cast<long long>(row) * ldr) : nullptr;
     const float mean = mean_in[row], rstd = rstd_in[row];
-    float4 dy[VPL], xh[VPL];
-    float s1 = 0.f, s2 = 0.f;
+    float4 dy[VPL], xh[VPL], rv[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int c4 = lane + 32 * i;
@@ -106,15 +114,18 @@ __global__ void __launch_bounds__(kLnWarps * 32)
         dy[i] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(dy_) + static_cast<long long>(row) * lddy +
                                                  4 * c4);
       }
-      const float4 xv = xr[c4];
-      xh[i] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
-      const float4 g = __ldg(g4 + c4);
+      xh[i] = xr[c4];
+      rv[i] = rr ? rr[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float4 g = __ldg(g4 + lane + 32 * i);
+      xh[i] = make_float4((xh[i].x - mean) * rstd, (xh[i].y - mean) * rstd, (xh[i].z - mean) * rstd,
+                          (xh[i].w - mean) * rstd);
       const float gx = dy[i].x * g.x, gy = dy[i].y * g.y, gz = dy[i].z * g.z, gw = dy[i].w * g.w;
       s1 += gx + gy + gz + gw;
       s2 += gx * xh[i].x + gy * xh[i].y + gz * xh[i].z + gw * xh[i].w;
-      acc_g[i].x += dy[i].x * xh[i].x; acc_g[i].y += dy[i].y * xh[i].y;
-      acc_g[i].z += dy[i].z * xh[i].z; acc_g[i].w += dy[i].w * xh[i].w;
-      acc_b[i].x += dy[i].x; acc_b[i].y += dy[i].y; acc_b[i].z += dy[i].z; acc_b[i].w += dy[i].w;
     }
     const float m1 = warp_sum(s1) * (1.0f / H);
     const float m2 = warp_sum(s2) * (1.0f / H);
@@ -123,37 +134,40 @@ __global__ void __launch_bounds__(kLnWarps * 32)
       const int c4 = lane + 32 * i;
       const float4 g = __ldg(g4 + c4);
       float4 d;
-      d.x = rstd * (dy[i].x * g.x - m1 - xh[i].x * m2);
-      d.y = rstd * (dy[i].y * g.y - m1 - xh[i].y * m2);
-      d.z = rstd * (dy[i].z * g.z - m1 - xh[i].z * m2);
-      d.w = rstd * (dy[i].w * g.w - m1 - xh[i].w * m2);
-      if (resid) {
-        const float4 r = *reinterpret_cast<const float4*>(resid + static_cast<long long>(row) * ldr + 4 * c4);
-        d.x += r.x; d.y += r.y; d.z += r.z; d.w += r.w;
-      }
+      d.x = rstd * (dy[i].x * g.x - m1 - xh[i].x * m2) + rv[i].x;
+      d.y = rstd * (dy[i].y * g.y - m1 - xh[i].y * m2) + rv[i].y;
+      d.z = rstd * (dy[i].z * g.z - m1 - xh[i].z * m2) + rv[i].z;
+      d.w = rstd * (dy[i].w * g.w - m1 - xh[i].w * m2) + rv[i].w;
       const long long off = static_cast<long long>(row) * lddx + 4 * c4;
       if (dx_f32) *reinterpret_cast<float4*>(dx_f32 + off) = d;
       if (dx_bf16) *reinterpret_cast<uint2*>(dx_bf16 + off) = make_uint2(pack_bf16x2(d.x, d.y), pack_bf16x2(d.z, d.w));
-      acc_c[i].x += d.x; acc_c[i].y += d.y; acc_c[i].z += d.z; acc_c[i].w += d.w;
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = 4 * (lane + 32 * i);
-    atomicAdd(&s_red[0][c + 0], acc_g[i].x); atomicAdd(&s_red[0][c + 1], acc_g[i].y);
-    atomicAdd(&s_red[0][c + 2], acc_g[i].z); atomicAdd(&s_red[0][c + 3], acc_g[i].w);
-    atomicAdd(&s_red[1][c + 0], acc_b[i].x); atomicAdd(&s_red[1][c + 1], acc_b[i].y);
-    atomicAdd(&s_red[1][c + 2], acc_b[i].z); atomicAdd(&s_red[1][c + 3], acc_b[i].w);
-    if (colsum) {
-      atomicAdd(&s_red[2][c + 0], acc_c[i].x); atomicAdd(&s_red[2][c + 1], acc_c[i].y);
-      atomicAdd(&s_red[2][c + 2], acc_c[i].z); atomicAdd(&s_red[2][c + 3], acc_c[i].w);
+      if (want_gb) {
+        float4 ag = acc_g[c4], ab = acc_b[c4];
+        ag.x += dy[i].x * xh[i].x; ag.y += dy[i].y * xh[i].y; ag.z += dy[i].z * xh[i].z; ag.w += dy[i].w * xh[i].w;
+        ab.x += dy[i].x; ab.y += dy[i].y; ab.z += dy[i].z; ab.w += dy[i].w;
+        acc_g[c4] = ag;
+        acc_b[c4] = ab;
+      }
+      if (want_cs) {
+        float4 ac = acc_c[c4];
+        ac.x += d.x; ac.y += d.y; ac.z += d.z; ac.w += d.w;
+        acc_c[c4] = ac;
+      }
     }
   }
   __syncthreads();
+  const float* sa = reinterpret_cast<const float*>(s_acc4);
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    if (dgamma) atomicAdd(dgamma + c, s_red[0][c]);
-    if (dbeta) atomicAdd(dbeta + c, s_red[1][c]);
-    if (colsum) atomicAdd(colsum + c, s_red[2][c]);
+    float tg = 0.f, tb = 0.f, tc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kLnWarps; ++w) {
+      tg += sa[(w * 3 + 0) * H + c];
+      tb += sa[(w * 3 + 1) * H + c];
+      tc += sa[(w * 3 + 2) * H + c];
+    }
+    if (dgamma) atomicAdd(dgamma + c, tg);
+    if (dbeta) atomicAdd(dbeta + c, tb);
+    if (colsum) atomicAdd(colsum + c, tc);
   }
 }
 
@@ -292,12 +306,24 @@ void layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch:
   const int grid = std::min((M + kLnWarps - 1) / kLnWarps, 2 * num_sms());
   dispatch_vpl(H, [&](auto vpl) {
     constexpr int V = decltype(vpl)::value;
+    const int smem = kLnWarps * 3 * V * 128 * static_cast<int>(sizeof(float));
+    static int configured_for[2] = {-1, -1};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_for[dy_bf16] != dev) {
+      if (dy_bf16) {
+        REVPP_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<V, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      } else {
+        REVPP_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<V, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      }
+      configured_for[dy_bf16] = dev;
+    }
     if (dy_bf16) {
-      ln_bwd_kernel<V, true><<<grid, kLnWarps * 32, 0, cur_stream()>>>(
+      ln_bwd_kernel<V, true><<<grid, kLnWarps * 32, smem, cur_stream()>>>(
           dy.data_ptr(), dy.stride(0), x.data_ptr<float>(), x.stride(0), gamma.data_ptr<float>(), mean.data_ptr<float>(),
           rstd.data_ptr<float>(), M, opt_f32(dgamma), opt_f32(dbeta), rp, ldr, dxf, dxb, lddx, opt_f32(colsum));
     } else {
-      ln_bwd_kernel<V, false><<<grid, kLnWarps * 32, 0, cur_stream()>>>(
+      ln_bwd_kernel<V, false><<<grid, kLnWarps * 32, smem, cur_stream()>>>(
           dy.data_ptr(), dy.stride(0), x.data_ptr<float>(), x.stride(0), gamma.data_ptr<float>(), mean.data_ptr<float>(),
           rstd.data_ptr<float>(), M, opt_f32(dgamma), opt_f32(dbeta), rp, ldr, dxf, dxb, lddx, opt_f32(colsum));
     }
