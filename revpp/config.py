@@ -193,8 +193,10 @@ def parse_args(argv=None) -> argparse.Namespace:
 
 def build_global_config(args: argparse.Namespace) -> GlobalConfig:
     """Namespace -> GlobalConfig with the reference's validation rules."""
-    if args.microbatch_size * args.num_microbatches != args.batch_size:
-        raise ValueError("batch_size must equal microbatch_size * num_microbatches")
+    # the reference's invariant (BERT/src/config.py:77-82); with pipeline replicas the batch
+    # is the global one, split evenly over the replicas
+    if args.microbatch_size * args.num_microbatches * max(args.dp, 1) != args.batch_size:
+        raise ValueError("batch_size must equal microbatch_size * num_microbatches * dp")
     if args.is_pareprop and not args.reversible:
         raise ValueError("is_pareprop=True requires reversible=True")
     if args.inverse and not args.reversible:

@@ -174,7 +174,7 @@ def test_pipeline_replicas_average_gradients():
     """PP = 2 x DP = 2 on 4 gloo ranks: after the replica all-reduce every stage holds the
     mean of the two replicas' gradients (each replica on its own local batch), and the
     optimizer step leaves both replicas with identical parameters."""
-    extra = "--reversible --dp 2"
+    extra = "--reversible --dp 2 --microbatch-size 2"
     world = 4
     gathered = _run(extra, world)
     cfg = _cfg(extra, world)
