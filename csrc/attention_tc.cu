@@ -10,7 +10,8 @@
 //                S_{j+1} is issued before waiting for P_j, so the tensor core works on the
 //                next scores while the softmax warps handle the current ones.
 //   warps 2-5  : softmax, one thread per query row: S row from TMEM, online max / sum in
-//                fp32 (exp2 with the 1/sqrt(d) * log2(e) scale folded in), P_j as bf16 into a
+//                fp32 (hardware exp2 with the 1/sqrt(d) * log2(e) scale folded into one FMA
+//                after the row max), P_j as bf16 into a
 //                128-byte-swizzled smem tile (the MMA's A operand), and O accumulated in
 //                registers: O = O * alpha_{j-1} + PV_{j-1}.
 // Shared memory ~97 KB and 256 TMEM columns, so two CTAs share an SM.
@@ -219,19 +220,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
+      // raw scores; the softmax scale (> 0) is applied after the max, folded into one FMA
       float sv[kKV];
 #pragma unroll
-      for (int c = 0; c < kKV; ++c) sv[c] = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
+      for (int c = 0; c < kKV; ++c) sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
       const int kbase = j * kKV;
       if (kbase + kKV > S) {
 #pragma unroll
         for (int c = 0; c < kKV; ++c)
           if (kbase + c >= S) sv[c] = -INFINITY;
       }
-      float mx = m;
+      float rmx = sv[0];
 #pragma unroll
-      for (int c = 0; c < kKV; ++c) mx = fmaxf(mx, sv[c]);
-      const float alpha = exp2f(m - mx);
+      for (int c = 1; c < kKV; ++c) rmx = fmaxf(rmx, sv[c]);
+      const float mx = fmaxf(m, rmx * sl2);
+      const float alpha = ex2_approx(m - mx);
       float rs = 0.f;
       l *= alpha;
       m = mx;
@@ -246,7 +249,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(sv[8 * c + 2 * e] - mx), p1 = exp2f(sv[8 * c + 2 * e + 1] - mx);
+          const float p0 = ex2_approx(fmaf(sv[8 * c + 2 * e], sl2, -mx));
+          const float p1 = ex2_approx(fmaf(sv[8 * c + 2 * e + 1], sl2, -mx));
           rs += p0 + p1;
           w[e] = pack_bf16x2(p0, p1);
         }
@@ -357,7 +361,8 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 //   dQ_j = dS K         (M 128 queries, N 64, K 128 keys; dS read MN-major from the dS^T
 //                        tile)                               -> TMEM cols [384, 448)
 //   dQ warps (one thread per query) add dQ_j * scale into an fp32 buffer with atomics.
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax / final dK dV, 6-9 dQ.
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK dV, 6-9 dQ,
+// 10-13 softmax (queries 64-127).
 // Overlap: as soon as the softmax of tile j has consumed S^T / dP^T, the issuer starts
 // S^T / dP^T of tile j+1 and only then the dV / dK / dQ MMAs of tile j, so the softmax of
 // tile j+1 runs while the tensor core works on tile j.  P^T and dS^T are therefore
@@ -365,7 +370,7 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 namespace {
 constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 448;
 constexpr uint32_t kTile = 128 * 64 * 2;       // 16 KB: a [128 x 64] bf16 tile
 constexpr uint32_t kSqTile = 2 * kTile;        // 32 KB: a [128 x 128] bf16 tile (2 swizzle chunks)
 struct BwdSmem {
@@ -413,7 +418,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* dq_empty = bar + 10;
   uint64_t* kv_done = bar + 11;
   uint64_t* drain = bar + 12;
-  uint64_t* grp_bar = bar + 13;   // the four softmax warps' own barrier (bounded waits)
+  uint64_t* grp_bar = bar + 13;   // the eight softmax warps' own barrier (bounded waits)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [128]
@@ -436,14 +441,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(&p_empty[0], 1);
     mbar_init(&p_empty[1], 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(kv_done, 1);
     mbar_init(drain, 1);
-    mbar_init(grp_bar, 4);
+    mbar_init(grp_bar, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -562,28 +567,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 6 || warp >= 10) {
     // ------------------------------------------------------------------ softmax (keys)
+    // Two warpgroups: warps 2-5 take queries [0, 64) of the tile, warps 10-13 [64, 128);
+    // each warp owns the 32 TMEM lanes (keys) of its quarter.
+    const int grp = warp >= 10 ? 1 : 0;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;      // key row within the tile
     const int tid = r;                      // 0..127 within this warpgroup
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const bool key_ok = k0 + r < S;
     const float ln2inv = 1.4426950408889634f;
+    const float4* s_lse4 = reinterpret_cast<const float4*>(s_lse);
+    const float4* s_D4 = reinterpret_cast<const float4*>(s_D);
     uint8_t* pt_base = smem + BwdSmem::pt;
     uint8_t* ds_base = smem + BwdSmem::dst;
     bool ok = true;
     uint32_t grp_phase = 0;
-    auto group_sync = [&]() -> bool {  // the four softmax warps, bounded
+    auto group_sync = [&]() -> bool {  // all eight softmax warps, bounded
       __syncwarp();
       if (lane == 0) mbar_arrive(grp_bar);
       const bool w = mbar_wait(grp_bar, grp_phase, args.status, abort_flag);
       grp_phase ^= 1u;
       return w;
     };
-    // LSE / D of the next query tile are fetched one tile ahead
-    float pre_lse = tid < S ? g_lse[tid] * ln2inv : 0.f;
-    float pre_D = tid < S ? g_D[tid] : 0.f;
+    // group 0 stages LSE (log2 units; +inf past the sequence end, so P = 0 there), group 1
+    // stages D; both one query tile ahead
+    auto fetch = [&](int q) -> float {
+      if (grp == 0) return q < S ? g_lse[q] * ln2inv : __int_as_float(0x7f800000);
+      return q < S ? g_D[q] : 0.f;
+    };
+    float pre = fetch(tid);
     for (int j = 0; j < nq; ++j) {
       const uint32_t jp = j & 1;
       const uint32_t pb = j & 1;
@@ -591,13 +605,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
-      s_lse[tid] = pre_lse;
-      s_D[tid] = pre_D;
-      {
-        const int qn = (j + 1) * kBQ + tid;
-        pre_lse = (j + 1 < nq && qn < S) ? g_lse[qn] * ln2inv : 0.f;
-        pre_D = (j + 1 < nq && qn < S) ? g_D[qn] : 0.f;
-      }
+      (grp == 0 ? s_lse : s_D)[tid] = pre;
+      if (j + 1 < nq) pre = fetch((j + 1) * kBQ + tid);
       if (!group_sync()) {
         ok = false;
         break;
@@ -612,35 +621,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       const int sw = r & 7;
-      uint8_t* prow = pt_base + pb * kSqTile + (r >> 3) * 1024 + sw * 128;
-      uint8_t* drow = ds_base + pb * kSqTile + (r >> 3) * 1024 + sw * 128;
+      // this group's 64 queries are 64-query swizzle chunk `grp` of the P^T / dS^T tiles
+      uint8_t* prow = pt_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
+      uint8_t* drow = ds_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
+      const float sl2 = args.scale_log2;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * grp + cc;  // 32-query chunk of the tile
         uint32_t sv[32], dp[32];
         tmem_ld32(tmem + lane_off + c * 32, sv);
         tmem_ld32(tmem + lane_off + 128 + c * 32, dp);
         tmem_wait_ld();
         uint32_t pw[16], dw[16];
+        if (key_ok) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int ql0 = c * 32 + e;
-          const bool v0 = key_ok && (j * kBQ + ql0 < S);
-          const bool v1 = key_ok && (j * kBQ + ql0 + 1 < S);
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[e]) * args.scale_log2 - s_lse[ql0]) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[e + 1]) * args.scale_log2 - s_lse[ql0 + 1]) : 0.f;
-          const uint32_t pp = pack_bf16x2(p0, p1);
-          const float2 pr = unpack_bf16x2(pp);
-          const float d0 = pr.x * (__uint_as_float(dp[e]) - s_D[ql0]);
-          const float d1 = pr.y * (__uint_as_float(dp[e + 1]) - s_D[ql0 + 1]);
-          pw[e >> 1] = pp;
-          dw[e >> 1] = pack_bf16x2(d0, d1);
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 L = s_lse4[c * 8 + e4];
+            const float4 Dq = s_D4[c * 8 + e4];
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 0]), sl2, -L.x));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 1]), sl2, -L.y));
+            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 2]), sl2, -L.z));
+            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 3]), sl2, -L.w));
+            const uint32_t pp0 = pack_bf16x2(p0, p1), pp1 = pack_bf16x2(p2, p3);
+            const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
+            pw[2 * e4] = pp0;
+            pw[2 * e4 + 1] = pp1;
+            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[4 * e4 + 0]) - Dq.x),
+                                     r0.y * (__uint_as_float(dp[4 * e4 + 1]) - Dq.y));
+            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[4 * e4 + 2]) - Dq.z),
+                                         r1.y * (__uint_as_float(dp[4 * e4 + 3]) - Dq.w));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pw[e] = dw[e] = 0u;
         }
-        // 32 queries = 64 bytes = four 16-byte units of the row, in chunk c >> 1
-        const int chunk = c >> 1;
+        // 32 queries = 64 bytes = four 16-byte units of the row
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const int u = (c & 1) * 4 + t;
-          const uint32_t off = chunk * kTile + ((u ^ sw) << 4);
+          const int u = cc * 4 + t;
+          const uint32_t off = (u ^ sw) << 4;
           *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * t], pw[4 * t + 1], pw[4 * t + 2], pw[4 * t + 3]);
           *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
         }
@@ -650,32 +669,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // final dK, dV for this warp's keys
-    if (ok && mbar_wait(kv_done, 0, args.status, abort_flag)) {
+    // final dK, dV for this warp's keys (group 0)
+    if (grp == 0 && ok && mbar_wait(kv_done, 0, args.status, abort_flag)) {
       tc_fence_after();
-      uint32_t dv[2][32], dk[2][32];
-      tmem_ld32(tmem + lane_off + 256, dv[0]);
-      tmem_ld32(tmem + lane_off + 288, dv[1]);
-      tmem_ld32(tmem + lane_off + 320, dk[0]);
-      tmem_ld32(tmem + lane_off + 352, dk[1]);
-      tmem_wait_ld();
-      if (key_ok) {
-        const long long ld = 3LL * H;
-        uint4* gk = reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + k0 + r) * ld + H + h * 64);
-        uint4* gv = reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + k0 + r) * ld + 2 * H + h * 64);
-        const float sc = args.scale;
+      const long long ld = 3LL * H;
+      const long long base = (static_cast<long long>(row0) + k0 + r) * ld + h * 64;
+      // dK (TMEM cols 320..383, scaled) then dV (256..319), 32 columns per load
+#pragma unroll 1
+      for (int part = 0; part < 4; ++part) {
+        const bool is_k = part < 2;
+        const int half = part & 1;
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + (is_k ? 320 : 256) + 32 * half, v);
+        tmem_wait_ld();
+        if (key_ok) {
+          const float sc = is_k ? args.scale : 1.f;
+          uint4* g = reinterpret_cast<uint4*>(args.dqkv + base + (is_k ? H : 2 * H) + 32 * half);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int c0 = 8 * u;
-          uint32_t kw[4], vw[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int cc = c0 + 2 * e;
-            kw[e] = pack_bf16x2(__uint_as_float(dk[cc >> 5][cc & 31]) * sc, __uint_as_float(dk[(cc + 1) >> 5][(cc + 1) & 31]) * sc);
-            vw[e] = pack_bf16x2(__uint_as_float(dv[cc >> 5][cc & 31]), __uint_as_float(dv[(cc + 1) >> 5][(cc + 1) & 31]));
+          for (int u = 0; u < 4; ++u) {
+            g[u] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * u + 0]) * sc, __uint_as_float(v[8 * u + 1]) * sc),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 2]) * sc, __uint_as_float(v[8 * u + 3]) * sc),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 4]) * sc, __uint_as_float(v[8 * u + 5]) * sc),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 6]) * sc, __uint_as_float(v[8 * u + 7]) * sc));
           }
-          gk[u] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-          gv[u] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         }
       }
     }
@@ -717,8 +733,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, int64_t M, int64_t S,
-                         int64_t heads);
+void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, torch::Tensor dq_acc,
+                         int64_t M, int64_t S, int64_t heads);
 void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H);
 
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
@@ -739,8 +755,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   REVPP_CHECK(dq_acc.numel() >= M * H && Dbuf.numel() >= B * heads * S, "scratch too small");
   c10::cuda::CUDAGuard guard(qkv.device());
   cudaStream_t st = cur_stream();
-  REVPP_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, M * H * sizeof(float), st));
-  attn_bwd_dot_launch(dout, out, Dbuf, M, S, heads);
+  attn_bwd_dot_launch(dout, out, Dbuf, dq_acc, M, S, heads);  // D, and dq_acc = 0
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
   const CUtensorMap tq = make_tmap_2d(qkv.data_ptr(), bf, 2, 3 * H, M, 3 * H * 2, 64, 128, sw);
@@ -782,7 +797,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
 namespace revpp {
 
 __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
-                                    float* __restrict__ D, int M, int S, int heads);
+                                    float* __restrict__ D, float* __restrict__ dq_acc, int M, int S, int heads);
 __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, long long M,
                                        int H);
 
@@ -865,15 +880,13 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
   } catch (const std::exception& ex) {
     return noalloc_fail(REVPP_NOALLOC_BAD_ARGUMENT, err, errlen, ex.what());
   }
-  e = cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(M * H) * sizeof(float), st);
-  if (e != cudaSuccess)
-    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("memset: ") + cudaGetErrorString(e));
   {
+    // D = rowsum(dO * O), and the dQ accumulator (which must start at zero) is cleared
     const long long threads = 256;
-    const long long blocks = (M * heads * 32 + threads - 1) / threads;
+    const long long blocks = (M * heads * 8 + threads - 1) / threads;
     attn_bwd_dot_kernel<<<static_cast<unsigned>(blocks), static_cast<unsigned>(threads), 0, st>>>(
-        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), Dbuf, static_cast<int>(M), S,
-        heads);
+        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), Dbuf, dq_acc,
+        static_cast<int>(M), S, heads);
   }
   AttnBwdTcArgs a;
   a.lse = lse;
