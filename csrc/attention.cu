@@ -238,22 +238,40 @@ __global__ void __launch_bounds__(kWarps * 32)
 }
 
 // ------------------------------------------------------------------ backward
-// D[b, h, s] = sum_d dO[s, h*64 + d] * O[s, h*64 + d]
+// Backward pre-pass: D[b, h, s] = sum_d dO[s, h*64 + d] * O[s, h*64 + d], and the fp32 dQ
+// accumulator slice of (s, h) is zeroed (when given).  Eight threads per (row, head), 16
+// bytes of dO and O each, so a warp reads four consecutive 128-byte head slices.
 __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
-                                    float* __restrict__ D, int M, int S, int heads) {
+                                    float* __restrict__ D, float* __restrict__ dq_acc, int M, int S, int heads) {
   const int H = heads * kD;
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int total = M * heads;
-  if (warp_global >= total) return;
-  const int row = warp_global / heads, h = warp_global % heads;
-  const long long off = static_cast<long long>(row) * H + h * kD + lane * 2;
-  const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + off));
-  const float2 c = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(out + off));
-  const float s = warp_sum(a.x * c.x + a.y * c.y);
-  if (lane == 0) {
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long pair = t >> 3;
+  const int sub = static_cast<int>(t & 7);
+  if (pair >= static_cast<long long>(M) * heads) return;  // whole groups of eight leave together
+  const int row = static_cast<int>(pair / heads), h = static_cast<int>(pair % heads);
+  const long long off = static_cast<long long>(row) * H + h * kD + sub * 8;
+  const uint4 a = *reinterpret_cast<const uint4*>(dout + off);
+  const uint4 c = *reinterpret_cast<const uint4*>(out + off);
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = unpack_bf16x2(aw[i]), y = unpack_bf16x2(cw[i]);
+    s = fmaf(x.x, y.x, s);
+    s = fmaf(x.y, y.y, s);
+  }
+  const unsigned mask = 0xffu << (threadIdx.x & 24);
+  s += __shfl_xor_sync(mask, s, 1);
+  s += __shfl_xor_sync(mask, s, 2);
+  s += __shfl_xor_sync(mask, s, 4);
+  if (sub == 0) {
     const int b = row / S, sidx = row % S;
     D[(static_cast<long long>(b) * heads + h) * S + sidx] = s;
+  }
+  if (dq_acc != nullptr) {
+    float4* z = reinterpret_cast<float4*>(dq_acc + off);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -467,14 +485,15 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bf
 }
 
 // ------------------------------------------------------------------ host side
-void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, int64_t M, int64_t S,
-                         int64_t heads) {
-  const long long warps = M * heads;
+void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, torch::Tensor dq_acc,
+                         int64_t M, int64_t S, int64_t heads) {
+  const long long threads_total = M * heads * 8;
   const int threads = 256;
-  const long long blocks = (warps * 32 + threads - 1) / threads;
+  const long long blocks = (threads_total + threads - 1) / threads;
   attn_bwd_dot_kernel<<<static_cast<unsigned>(blocks), threads, 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
-      D.data_ptr<float>(), static_cast<int>(M), static_cast<int>(S), static_cast<int>(heads));
+      D.data_ptr<float>(), dq_acc.defined() ? dq_acc.data_ptr<float>() : nullptr, static_cast<int>(M),
+      static_cast<int>(S), static_cast<int>(heads));
   REVPP_CHECK_LAUNCH();
 }
 
@@ -524,16 +543,7 @@ void attn_bwd(const torch::Tensor& qkv, const torch::Tensor& out, const torch::T
   cudaStream_t st = cur_stream();
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kD)));
   const float scale_log2 = static_cast<float>(1.4426950408889634) * scale;
-  REVPP_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, M * H * sizeof(float), st));
-  {
-    const long long warps = M * heads;
-    const int threads = 256;
-    const long long blocks = (warps * 32 + threads - 1) / threads;
-    attn_bwd_dot_kernel<<<static_cast<unsigned>(blocks), threads, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
-        Dbuf.data_ptr<float>(), static_cast<int>(M), static_cast<int>(S), static_cast<int>(heads));
-    REVPP_CHECK_LAUNCH();
-  }
+  attn_bwd_dot_launch(dout, out, Dbuf, dq_acc, M, S, heads);  // D, and dq_acc = 0
   dim3 grid(static_cast<unsigned>((S + kTileK - 1) / kTileK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
   constexpr int smem = 7 * 64 * 64 * 2 + 4 * 64 * 4;
   static int configured_for = -1;
