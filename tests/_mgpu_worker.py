@@ -129,6 +129,11 @@ def main():
         dist.broadcast(other, src=0)
         out["replica_diff"] = float((other - p_fused).abs().max())
     out["status"] = C.status_read_and_clear()
+    # one file per rank: concurrent ranks interleave their lines on a shared stdout
+    res_dir = os.environ.get("REVPP_MGPU_RESULT_DIR")
+    if res_dir:
+        with open(os.path.join(res_dir, f"rank{out['rank']}.json"), "w") as fh:
+            json.dump(out, fh)
     print("RESULT " + json.dumps(out), flush=True)
     tr.close()
     dist.barrier()

@@ -85,7 +85,7 @@ def test_checkpoint_round_trip_with_reference_alias_keys(tmp_path):
     from revpp.utils.env import build_env
 
     cfg = _cfg(f"--preset tiny-bert --num-hidden-layers 2 --device cpu --batch-size 8 --microbatch-size 4 "
-               f"--num-microbatches 2 --reversible --lr 1e-3 --checkpoint-dir {tmp_path}")
+               f"--num-microbatches 2 --reversible --lr 1e-3 --checkpoint-dir {tmp_path} --log-dir {tmp_path}/logs")
     env = build_env(cfg)
     tr = Trainer(cfg, env)
     batch = SyntheticBatches(cfg, 8, 1, seed=1).make(0)

@@ -1,9 +1,11 @@
 """Multi-GPU tests (NCCL, one process per GPU).  Skipped with fewer than 2 GPUs."""
 import json
 import os
+import shutil
 import socket
 import subprocess
 import sys
+import tempfile
 
 import pytest
 import torch
@@ -26,7 +28,8 @@ def _run(mode, n=2, timeout=240):
         pytest.skip(f"needs {n} GPUs")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "_mgpu_worker.py"), mode]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res_dir = tempfile.mkdtemp(prefix="revpp_mgpu_")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", REVPP_MGPU_RESULT_DIR=res_dir)
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
     if p.returncode != 0:
         out_dir = os.path.join(os.environ.get("GRAFT_REPO_ROOT", os.path.dirname(HERE)), "gpurun_out")
@@ -34,7 +37,12 @@ def _run(mode, n=2, timeout=240):
             with open(os.path.join(out_dir, f"mgpu_{mode}_fail.log"), "w") as fh:
                 fh.write(p.stdout + "\n----- stderr -----\n" + p.stderr)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
-    res = [json.loads(l[len("RESULT "):]) for l in p.stdout.splitlines() if l.startswith("RESULT ")]
+    res = []
+    for name in sorted(os.listdir(res_dir)):
+        with open(os.path.join(res_dir, name)) as fh:
+            res.append(json.load(fh))
+    shutil.rmtree(res_dir, ignore_errors=True)
+    assert len(res) == n, p.stdout[-2000:]
     return sorted(res, key=lambda r: r["rank"])
 
 
