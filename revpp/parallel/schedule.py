@@ -22,17 +22,18 @@ Action = Tuple[str, int]
 
 
 def one_f_one_b(stage: int, num_stages: int, n: int) -> List[Action]:
+    """1F1B as Schedule1F1B runs it (BERT/pipelining/schedules.py:708-852): min(n, P - s)
+    warm-up forwards, then alternate one backward and one forward (1B1F), then the
+    remaining backwards."""
     warmup = min(num_stages - stage, n)
     acts: List[Action] = [("F", i) for i in range(warmup)]
     f, b = warmup, 0
-    while f < n:
-        acts.append(("F", f))
-        f += 1
-        acts.append(("B", b))
-        b += 1
     while b < n:
         acts.append(("B", b))
         b += 1
+        if f < n:
+            acts.append(("F", f))
+            f += 1
     return acts
 
 
@@ -47,9 +48,11 @@ def forward_only(stage: int, num_stages: int, n: int) -> List[Action]:
 SCHEDULES = {"1f1b": one_f_one_b, "gpipe": gpipe}
 
 
-def simulate(num_stages: int, n: int, schedule: str = "1f1b", t_f: float = 1.0, t_b: float = 2.0):
+def simulate(num_stages: int, n: int, schedule: str = "1f1b", t_f: float = 1.0, t_b: float = 2.0,
+             events: list | None = None):
     """Event simulation of a schedule: returns (makespan, per-stage busy time).  Used to
-    check schedules without GPUs and to predict bubble fractions."""
+    check schedules without GPUs and to predict bubble fractions.  With ``events`` given,
+    every simulated action is appended as (stage, kind, micro-batch, start, end)."""
     fn = SCHEDULES[schedule]
     acts = [fn(s, num_stages, n) for s in range(num_stages)]
     pos = [0] * num_stages
@@ -72,6 +75,8 @@ def simulate(num_stages: int, n: int, schedule: str = "1f1b", t_f: float = 1.0, 
                 t[s] = start + t_f
                 f_done[s][i] = t[s]
                 busy[s] += t_f
+                if events is not None:
+                    events.append((s, "F", i, start, t[s]))
             else:
                 dep = f_done[s][i] if s == num_stages - 1 else b_done[s + 1][i]
                 if dep is None or f_done[s][i] is None:
@@ -80,11 +85,34 @@ def simulate(num_stages: int, n: int, schedule: str = "1f1b", t_f: float = 1.0, 
                 t[s] = start + t_b
                 b_done[s][i] = t[s]
                 busy[s] += t_b
+                if events is not None:
+                    events.append((s, "B", i, start, t[s]))
             pos[s] += 1
             progress = True
     if any(p < len(a) for p, a in zip(pos, acts)):
         raise RuntimeError("schedule deadlocks")
     return max(t), busy
+
+
+def dump_chrometrace(num_stages: int, n: int, path, schedule: str = "1f1b", t_f: float = 1.0,
+                     t_b: float = 2.0) -> float:
+    """Write the simulated schedule as a Chrome trace (one row per stage, one slice per
+    forward / backward of a micro-batch, times in the units of ``t_f`` / ``t_b`` read as
+    milliseconds), the counterpart of the reference's schedule trace dump
+    (BERT/pipelining/schedules.py:2585).  Returns the makespan."""
+    import json
+
+    events: list = []
+    makespan, _ = simulate(num_stages, n, schedule, t_f, t_b, events)
+    trace = [{"name": "process_name", "ph": "M", "pid": 0, "args": {"name": f"{schedule} schedule"}}]
+    trace += [{"name": "thread_name", "ph": "M", "pid": 0, "tid": s, "args": {"name": f"stage {s}"}}
+              for s in range(num_stages)]
+    for s, kind, i, start, end in events:
+        trace.append({"name": f"{kind}{i}", "cat": "forward" if kind == "F" else "backward", "ph": "X", "pid": 0,
+                      "tid": s, "ts": start * 1e3, "dur": (end - start) * 1e3})
+    with open(path, "w") as fh:
+        json.dump({"traceEvents": trace}, fh)
+    return makespan
 
 
 class PipelineExecutor:
