@@ -259,11 +259,41 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// erf(z) and exp(-z^2) together, branch-free, after Abramowitz & Stegun, Handbook of
+// Mathematical Functions (1964), formula 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),
+// for z >= 0 with |error| <= 1.5e-7 (odd extension for z < 0).  One reciprocal and one
+// exp2 on the special-function unit, six FMAs: cheaper than a general erff in the GEMM
+// epilogues, where the GELU of every output element is computed.
+__device__ __forceinline__ float erf_and_gauss(float z, float& gauss) {
+  const float az = fabsf(z);
+  const float t = rcp_approx(fmaf(0.3275911f, az, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  gauss = ex2_approx(-az * az * 1.4426950408889634f);  // exp(-z^2)
+  return copysignf(fmaf(-poly, gauss, 1.0f), z);
+}
+
+// GELU with the exact (erf) form, x * Phi(x), and its derivative Phi(x) + x * phi(x);
+// phi(x) = exp(-x^2 / 2) / sqrt(2 pi) reuses the exponential of the erf evaluation.
+__device__ __forceinline__ float gelu_erf(float x) {
+  float g;
+  const float e = erf_and_gauss(x * 0.70710678118654752f, g);
+  return 0.5f * x * (1.0f + e);
+}
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-  const float pdf = 0.39894228040143268f * expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  float g;
+  const float e = erf_and_gauss(x * 0.70710678118654752f, g);
+  return fmaf(x * 0.39894228040143268f, g, 0.5f * (1.0f + e));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
