@@ -399,7 +399,24 @@ struct AttnBwdTcArgs {
   int S, heads;
   float scale, scale_log2;
   int* status;
+  float* colsum = nullptr;  // [3H] fp32 or null: += column sums of the bf16 dK / dV written here
 };
+
+// Column sums over the 32 rows (lanes) of a warp: v holds this lane's 32 columns; returns
+// the sum of column `lane` (recursive halving: 31 shuffles instead of 32 x 5).
+__device__ __forceinline__ float warp_column_sums32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? v[i] : v[i + w];
+      const float keep = up ? v[i + w] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0];
+}
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
@@ -669,8 +686,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // final dK, dV for this warp's keys (group 0)
-    if (grp == 0 && ok && mbar_wait(kv_done, 0, args.status, abort_flag)) {
+    // final dK, dV for this warp's keys (group 0); the decision is made warp-uniform since
+    // the column sums below shuffle across all lanes
+    bool fin = grp == 0 && ok;
+    if (fin) fin = mbar_wait(kv_done, 0, args.status, abort_flag);
+    if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       const long long ld = 3LL * H;
       const long long base = (static_cast<long long>(row0) + k0 + r) * ld + h * 64;
@@ -682,16 +702,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t v[32];
         tmem_ld32(tmem + lane_off + (is_k ? 320 : 256) + 32 * half, v);
         tmem_wait_ld();
-        if (key_ok) {
-          const float sc = is_k ? args.scale : 1.f;
-          uint4* g = reinterpret_cast<uint4*>(args.dqkv + base + (is_k ? H : 2 * H) + 32 * half);
+        const float sc = is_k ? args.scale : 1.f;
+        uint32_t pk[16];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            g[u] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * u + 0]) * sc, __uint_as_float(v[8 * u + 1]) * sc),
-                              pack_bf16x2(__uint_as_float(v[8 * u + 2]) * sc, __uint_as_float(v[8 * u + 3]) * sc),
-                              pack_bf16x2(__uint_as_float(v[8 * u + 4]) * sc, __uint_as_float(v[8 * u + 5]) * sc),
-                              pack_bf16x2(__uint_as_float(v[8 * u + 6]) * sc, __uint_as_float(v[8 * u + 7]) * sc));
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * sc, __uint_as_float(v[2 * e + 1]) * sc);
+        const int gcol = (is_k ? H : 2 * H) + h * 64 + 32 * half;
+        if (key_ok) {
+          uint4* g = reinterpret_cast<uint4*>(args.dqkv + base - h * 64 + gcol);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) g[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+        if (args.colsum != nullptr) {  // bias gradient of the K / V projections
+          float cv[32];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float2 r2 = unpack_bf16x2(pk[e]);
+            cv[2 * e] = key_ok ? r2.x : 0.f;
+            cv[2 * e + 1] = key_ok ? r2.y : 0.f;
           }
+          atomicAdd(args.colsum + gcol + lane, warp_column_sums32(cv, lane));
         }
       }
     }
@@ -737,9 +767,36 @@ void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, to
                          int64_t M, int64_t S, int64_t heads);
 void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H);
 
+// dqkv[:, 0:H] = bf16(dq_acc) and colsum[0:H] += column sums of those bf16 values.  Each
+// block walks a strided set of rows with one thread per 4 columns, so every column sum is
+// added once per block.
+__global__ void attn_dq_convert_colsum_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
+                                              long long M, int H, float* __restrict__ colsum) {
+  const int n4 = H / 4;
+  for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (long long row = blockIdx.x; row < M; row += gridDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(dq_acc + row * H)[c4];
+      const uint32_t p0 = pack_bf16x2(v.x, v.y), p1 = pack_bf16x2(v.z, v.w);
+      *reinterpret_cast<uint2*>(dqkv + row * 3LL * H + 4 * c4) = make_uint2(p0, p1);
+      const float2 r0 = unpack_bf16x2(p0), r1 = unpack_bf16x2(p1);
+      s0 += r0.x;
+      s1 += r0.y;
+      s2 += r1.x;
+      s3 += r1.y;
+    }
+    atomicAdd(colsum + 4 * c4 + 0, s0);
+    atomicAdd(colsum + 4 * c4 + 1, s1);
+    atomicAdd(colsum + 4 * c4 + 2, s2);
+    atomicAdd(colsum + 4 * c4 + 3, s3);
+  }
+}
+
+// colsum (optional, fp32 [3H]): += column sums of the bf16 dqkv, the q/k/v projection bias
+// gradient, fused into the dK/dV write-out and the dQ conversion.
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
-                 int64_t S, int64_t heads) {
+                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum) {
   check_cuda_bf16(qkv, "qkv");
   check_cuda_bf16(out, "out");
   check_cuda_bf16(dout, "dout");
@@ -770,6 +827,13 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   a.scale = static_cast<float>(1.0 / std::sqrt(64.0));
   a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
   a.status = status_device_ptr();
+  float* cs = nullptr;
+  if (colsum.has_value() && colsum->defined()) {
+    check_cuda_f32(*colsum, "colsum");
+    REVPP_CHECK(colsum->is_contiguous() && colsum->numel() >= 3 * H, "colsum must hold 3H floats");
+    cs = colsum->data_ptr<float>();
+  }
+  a.colsum = cs;
   constexpr int smem = BwdSmem::total + 1024;
   static int configured_for = -1;
   int dev = 0;
@@ -781,7 +845,15 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
   attn_bwd_tc_kernel<<<grid, kBwdThreads, smem, st>>>(tq, tdo, a);
   REVPP_CHECK_LAUNCH();
-  attn_dq_convert_launch(dq_acc, dqkv, M, H);
+  if (cs == nullptr) {
+    attn_dq_convert_launch(dq_acc, dqkv, M, H);
+  } else {
+    const int blocks = static_cast<int>(std::min<int64_t>(M, 4 * num_sms()));
+    attn_dq_convert_colsum_kernel<<<blocks, 256, 0, st>>>(dq_acc.data_ptr<float>(),
+                                                          reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), M,
+                                                          static_cast<int>(H), cs);
+    REVPP_CHECK_LAUNCH();
+  }
 }
 
 }  // namespace revpp

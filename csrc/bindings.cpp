@@ -10,7 +10,8 @@ namespace revpp {
 void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
              int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
              const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
-             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant);
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant,
+             const c10::optional<torch::Tensor>& colsum);
 int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K);
 // norm.cu
 void layernorm_fwd(const torch::Tensor& x, const torch::Tensor& gamma, const torch::Tensor& beta, double eps,
@@ -51,7 +52,7 @@ void ipc_close(int64_t base);
 std::vector<std::string> ipc_export(const torch::Tensor& t);
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
-                 int64_t S, int64_t heads);
+                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum);
 // embed_head.cu
 void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
                     const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
@@ -100,7 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &revpp::gemm_tc, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("C"),
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("aux_out") = py::none(),
-        py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1, py::arg("variant") = 0);
+        py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1, py::arg("variant") = 0,
+        py::arg("colsum") = py::none());
   m.def("gemm_suggest_splits", &revpp::gemm_suggest_splits);
 
   m.def("layernorm_fwd", &revpp::layernorm_fwd, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps"),
@@ -114,7 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("heads"));
   m.def("attn_bwd_tc", &revpp::attn_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
-        py::arg("dqkv"), py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
+        py::arg("dqkv"), py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"),
+        py::arg("colsum") = py::none());
   m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
         py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("bert_embed_fwd", &revpp::bert_embed_fwd);

@@ -45,6 +45,7 @@ struct GemmArgs {
   const float* resid;  // [M, ld_resid] fp32 (kEpiResid)
   long long ld_resid;
   float sign;
+  float* colsum;  // [N] fp32 or null: kEpiDGelu adds the column sums of its (bf16) output
   int* status;
 };
 
@@ -190,6 +191,9 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
     }
     epi_stage_row<true>(stg, lane, v);
     __syncwarp();
+    float cs[8];  // column sums of the rounded outputs (bias gradient of the producing layer)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cs[e] = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rr = 4 * i + (lane >> 3);
@@ -203,9 +207,24 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
           const float2 g = unpack_bf16x2(wa[e]);
           const float2 pre = unpack_bf16x2(xa[e]);
           o[e] = pack_bf16x2(g.x * gelu_erf_grad(pre.x), g.y * gelu_erf_grad(pre.y));
+          const float2 r = unpack_bf16x2(o[e]);
+          cs[2 * e] += r.x;
+          cs[2 * e + 1] += r.y;
         }
         *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
             make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (a.colsum != nullptr) {  // warp-uniform
+      // lanes u, u+8, u+16, u+24 hold the same 8 columns for different rows
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 8);
+        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 16);
+      }
+      if (lane < 8 && col < a.N) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(a.colsum + col + e, cs[e]);
       }
     }
   } else if constexpr (EPI == kEpiAtomicF32) {
@@ -772,7 +791,8 @@ void dispatch_gemm(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const C
 void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn, int64_t M, int64_t N, int64_t K,
              int64_t epi, torch::Tensor C, const c10::optional<torch::Tensor>& bias,
              const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
-             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant) {
+             const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant,
+             const c10::optional<torch::Tensor>& colsum) {
   check_cuda_bf16(A, "A");
   check_cuda_bf16(B, "B");
   REVPP_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm operands must be 2-D");
@@ -848,6 +868,13 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
     args.ld_resid = resid->stride(0);
   }
   args.sign = static_cast<float>(sign);
+  args.colsum = nullptr;
+  if (colsum.has_value() && colsum->defined()) {
+    REVPP_CHECK(epi == kEpiDGelu, "the fused column sum is implemented for the GELU-backward epilogue only");
+    check_cuda_f32(*colsum, "colsum");
+    REVPP_CHECK(colsum->is_contiguous() && colsum->numel() >= N, "colsum must hold N floats");
+    args.colsum = colsum->data_ptr<float>();
+  }
   args.status = status_device_ptr();
 
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

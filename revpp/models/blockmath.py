@@ -236,8 +236,8 @@ class KernelMath:
             dy_bf16 = self.scratch("g_dyb", (M, H), torch.bfloat16)
             ops.cast_colsum(dy2d, out=dy_bf16, colsum=w.d_b2)           # bf16(dy), db2 += sum(dy)
         ops.linear_wgrad(dy_bf16, ctx.h, w.d_w2)                        # dW2 += dy^T h
-        ops.linear_dgrad(dy_bf16, w.w2, du, epi=ops.EPI_DGELU, aux=ctx.u)  # du = (dy W2) * gelu'(u)
-        ops.cast_colsum(du, colsum=w.d_b1)                              # db1 += sum(du)
+        # du = (dy W2) * gelu'(u), db1 += sum(du) in the same epilogue
+        ops.linear_dgrad(dy_bf16, w.w2, du, epi=ops.EPI_DGELU, aux=ctx.u, colsum=w.d_b1)
         ops.linear_wgrad(du, ctx.b, w.d_w1)                             # dW1 += du^T LN2(x)
         ops.linear_dgrad(du, w.w1, dln)                                 # d LN2 out = du W1
         if out is None:
@@ -274,8 +274,8 @@ class KernelMath:
         dln = self.scratch("f_dln", (M, H), torch.bfloat16)
         ops.linear_wgrad(dy_bf16, ctx.o, w.d_wo)                        # dWo += dy^T o
         ops.linear_dgrad(dy_bf16, w.wo, do)                             # do = dy Wo
-        ops.attention_bwd(ctx.qkv, ctx.o, do, ctx.lse, dqkv, dq_acc, dbuf, B, S, self.heads)
-        ops.cast_colsum(dqkv, colsum=w.d_bqkv)                          # dbqkv += sum(dqkv)
+        # dqkv, and dbqkv += sum(dqkv) fused into the attention backward's write-out
+        ops.attention_bwd(ctx.qkv, ctx.o, do, ctx.lse, dqkv, dq_acc, dbuf, B, S, self.heads, colsum=w.d_bqkv)
         ops.linear_wgrad(dqkv, ctx.a, w.d_wqkv)                         # dWqkv += dqkv^T LN1(x)
         ops.linear_dgrad(dqkv, w.wqkv, dln)                             # d LN1 out = dqkv Wqkv
         if out is None:

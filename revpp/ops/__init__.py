@@ -37,11 +37,12 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[t
 
 
 def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int = EPI_BF16,
-                 aux: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out[M, K] = epi(dy[M, N] @ w[N, K])   (input gradient; w read MN-major)."""
+                 aux: Optional[torch.Tensor] = None, colsum: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, K] = epi(dy[M, N] @ w[N, K])   (input gradient; w read MN-major).  With the
+    GELU-backward epilogue, ``colsum`` (fp32 [K]) accumulates the column sums of ``out``."""
     M, N = dy.shape
     K = w.shape[1]
-    ext().gemm_tc(dy, False, w, True, M, K, N, epi, out, aux=aux)
+    ext().gemm_tc(dy, False, w, True, M, K, N, epi, out, aux=aux, colsum=colsum)
     return out
 
 
@@ -82,12 +83,16 @@ def attention_fwd(qkv, out, lse, B, S, heads):
         ext().attn_fwd(qkv, out, lse, B, S, heads)
 
 
-def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads):
-    """Flash attention backward (tcgen05; REVPP_ATTN_TC=0 selects the mma.sync kernel)."""
+def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads, colsum=None):
+    """Flash attention backward (tcgen05; REVPP_ATTN_TC=0 selects the mma.sync kernel).
+    ``colsum`` (fp32 [3H]) accumulates the column sums of dqkv (the in-projection bias
+    gradient); the tcgen05 path fuses it into its write-out."""
     if _ATTN_TC:
-        ext().attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads)
+        ext().attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads, colsum=colsum)
     else:
         ext().attn_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads)
+        if colsum is not None:
+            cast_colsum(dqkv, colsum=colsum)
 
 
 __all__ = [

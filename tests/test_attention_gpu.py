@@ -84,7 +84,11 @@ def test_attn_bwd_tcgen05(B, S, heads):
     dq_acc = torch.empty(B * S, H, device="cuda")
     D = torch.empty(B, heads, S, device="cuda")
     dqkv = torch.empty_like(qkv)
-    C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, D, B, S, heads)
+    cs = torch.full((3 * H,), -0.5, device="cuda")
+    C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq_acc, D, B, S, heads, colsum=cs)
+    torch.cuda.synchronize()
+    ref_cs = dqkv.double().sum(0) - 0.5  # fused bias gradient = column sums of the bf16 dqkv
+    assert (cs.double() - ref_cs).abs().max().item() <= 1e-4 * (1 + ref_cs.abs().max().item())
     dqkv2 = torch.empty_like(qkv)
     C.attn_bwd(qkv, out, dout, lse, dqkv2, dq_acc, D, B, S, heads)
     torch.cuda.synchronize()

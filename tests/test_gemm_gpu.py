@@ -93,12 +93,16 @@ def test_dgelu(M, N, K, variant):
     a, w = _rand(M, K), _rand(K, N, scale=0.05)
     u = _rand(M, N)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u, variant=variant)
+    cs = torch.full((N,), 0.25, device="cuda")
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u, variant=variant, colsum=cs)
     torch.cuda.synchronize()
     ud = u.double()
     dg = 0.5 * (1 + torch.erf(ud / math.sqrt(2))) + ud * torch.exp(-0.5 * ud * ud) / math.sqrt(2 * math.pi)
     dh = (a.double() @ w.double()).to(torch.bfloat16).double()
     _close(out, dh * dg, 2e-2)
+    # fused bias gradient: column sums of the bf16 output, added to what colsum held
+    ref_cs = out.double().sum(0) + 0.25
+    assert (cs.double() - ref_cs).abs().max().item() <= 1e-4 * (1 + ref_cs.abs().max().item())
 
 
 WGRAD_SHAPES = [(128, 256, 64), (256, 512, 256), (96, 160, 197 * 3), (1024, 1024, 1000), (3072, 1024, 4096)]
