@@ -438,6 +438,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* grp_bar = bar + 13;   // the eight softmax warps' own barrier (bounded waits)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* cs_bar = bar + 16;    // the four dK / dV warps' column sums are in shared memory
   float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [128]
   float* s_D = s_lse + 128;                                            // [128]
 
@@ -466,6 +467,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(kv_done, 1);
     mbar_init(drain, 1);
     mbar_init(grp_bar, 8);
+    mbar_init(cs_bar, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -721,7 +723,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             cv[2 * e] = key_ok ? r2.x : 0.f;
             cv[2 * e + 1] = key_ok ? r2.y : 0.f;
           }
-          atomicAdd(args.colsum + gcol + lane, warp_column_sums32(cv, lane));
+          // this warp's 32 keys; the P^T buffers are free once kv_done has fired
+          reinterpret_cast<float*>(smem + BwdSmem::pt)[quarter * 128 + part * 32 + lane] =
+              warp_column_sums32(cv, lane);
+        }
+      }
+      if (args.colsum != nullptr) {
+        // One atomic per column and CTA: the 4 warps' sums are added here first (an atomic
+        // per warp put 4 x (B * S / 128) same-address atomics in L2's queue per column).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cs_bar);
+        if (quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
+          const float* red = reinterpret_cast<const float*>(smem + BwdSmem::pt);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = i * 32 + lane;  // 0..63 dK columns, 64..127 dV columns
+            const float sum = red[c] + red[128 + c] + red[256 + c] + red[384 + c];
+            atomicAdd(args.colsum + (c < 64 ? H : 2 * H - 64) + h * 64 + c, sum);
+          }
         }
       }
     }
@@ -767,28 +786,53 @@ void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, to
                          int64_t M, int64_t S, int64_t heads);
 void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H);
 
-// dqkv[:, 0:H] = bf16(dq_acc) and colsum[0:H] += column sums of those bf16 values.  Each
-// block walks a strided set of rows with one thread per 4 columns, so every column sum is
-// added once per block.
-__global__ void attn_dq_convert_colsum_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
-                                              long long M, int H, float* __restrict__ colsum) {
-  const int n4 = H / 4;
-  for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    for (long long row = blockIdx.x; row < M; row += gridDim.x) {
-      const float4 v = reinterpret_cast<const float4*>(dq_acc + row * H)[c4];
-      const uint32_t p0 = pack_bf16x2(v.x, v.y), p1 = pack_bf16x2(v.z, v.w);
-      *reinterpret_cast<uint2*>(dqkv + row * 3LL * H + 4 * c4) = make_uint2(p0, p1);
-      const float2 r0 = unpack_bf16x2(p0), r1 = unpack_bf16x2(p1);
-      s0 += r0.x;
-      s1 += r0.y;
-      s2 += r1.x;
-      s3 += r1.y;
+// dqkv[:, 0:H] = bf16(dq_acc) and colsum[0:H] += column sums of those bf16 values.
+__global__ void __launch_bounds__(256) attn_dq_convert_colsum_kernel(const float* __restrict__ dq_acc,
+                                                                      __nv_bfloat16* __restrict__ dqkv, long long M,
+                                                                      int H, float* __restrict__ colsum) {
+  // Block (x, y) converts rows [r0, r1) of the 256 columns [256 y, 256 y + 256): 64 threads
+  // per row (one 16-byte group each) x 4 rows, 16 loads in flight per thread.  The four
+  // row-lanes' sums meet in shared memory, so each column gets one atomic per row block
+  // (gridDim.x of them): a same-address atomic per 4-column group of every block of a
+  // grid spanning all rows serialised in L2 and tripled this kernel's time.
+  constexpr int U = 16;
+  __shared__ float4 red[4][64];
+  const int cg = threadIdx.x & 63;   // 4-column group within the slice
+  const int rl = threadIdx.x >> 6;   // row lane 0..3
+  const int c4 = blockIdx.y * 64 + cg;
+  const long long rows_per = (M + gridDim.x - 1) / gridDim.x;
+  const long long r0 = blockIdx.x * rows_per;
+  const long long r1 = r0 + rows_per < M ? r0 + rows_per : M;
+  const bool col_ok = 4 * c4 < H;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col_ok) {
+    for (long long row = r0 + rl; row < r1; row += 4 * U) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long rr = row + 4LL * u;
+        v[u] = rr < r1 ? __ldcs(reinterpret_cast<const float4*>(dq_acc + rr * H) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long rr = row + 4LL * u;
+        if (rr >= r1) break;
+        const uint32_t p0 = pack_bf16x2(v[u].x, v[u].y), p1 = pack_bf16x2(v[u].z, v[u].w);
+        *reinterpret_cast<uint2*>(dqkv + rr * 3LL * H + 4 * c4) = make_uint2(p0, p1);
+        const float2 q0 = unpack_bf16x2(p0), q1 = unpack_bf16x2(p1);
+        s.x += q0.x;
+        s.y += q0.y;
+        s.z += q1.x;
+        s.w += q1.y;
+      }
     }
-    atomicAdd(colsum + 4 * c4 + 0, s0);
-    atomicAdd(colsum + 4 * c4 + 1, s1);
-    atomicAdd(colsum + 4 * c4 + 2, s2);
-    atomicAdd(colsum + 4 * c4 + 3, s3);
+  }
+  red[rl][cg] = s;
+  __syncthreads();
+  if (rl == 0 && col_ok && r0 < r1) {
+    const float4 a = red[0][cg], b = red[1][cg], c = red[2][cg], d = red[3][cg];
+    atomicAdd(reinterpret_cast<float4*>(colsum + 4 * c4),
+              make_float4(a.x + b.x + c.x + d.x, a.y + b.y + c.y + d.y, a.z + b.z + c.z + d.z, a.w + b.w + c.w + d.w));
   }
 }
 
@@ -831,6 +875,8 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   if (colsum.has_value() && colsum->defined()) {
     check_cuda_f32(*colsum, "colsum");
     REVPP_CHECK(colsum->is_contiguous() && colsum->numel() >= 3 * H, "colsum must hold 3H floats");
+    REVPP_CHECK((reinterpret_cast<uintptr_t>(colsum->data_ptr()) & 15) == 0,
+                "colsum must be 16-byte aligned (vector atomics)");
     cs = colsum->data_ptr<float>();
   }
   a.colsum = cs;
@@ -848,8 +894,10 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   if (cs == nullptr) {
     attn_dq_convert_launch(dq_acc, dqkv, M, H);
   } else {
-    const int blocks = static_cast<int>(std::min<int64_t>(M, 4 * num_sms()));
-    attn_dq_convert_colsum_kernel<<<blocks, 256, 0, st>>>(dq_acc.data_ptr<float>(),
+    const unsigned slices = static_cast<unsigned>((H + 255) / 256);
+    const unsigned row_blocks =
+        static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(M / 64, num_sms() / slices)));
+    attn_dq_convert_colsum_kernel<<<dim3(row_blocks, slices), 256, 0, st>>>(dq_acc.data_ptr<float>(),
                                                           reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), M,
                                                           static_cast<int>(H), cs);
     REVPP_CHECK_LAUNCH();

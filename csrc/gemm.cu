@@ -18,6 +18,8 @@
 //
 // Replaces the reference's cuBLAS GEMMs inside nn.Linear / nn.MultiheadAttention
 // (BERT/models/bert_blocks.py:34-63) and their autograd backward.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host.h"
 
@@ -46,8 +48,23 @@ struct GemmArgs {
   long long ld_resid;
   float sign;
   float* colsum;  // [N] fp32 or null: kEpiDGelu adds the column sums of its (bf16) output
+  int chunked;    // 1: each CTA (pair) takes a contiguous run of tiles instead of every grid-th
   int* status;
 };
+
+// Tiles of one CTA (or CTA pair) `id` of `n`: either every n-th tile, or - with
+// `chunked` - a contiguous run, so consecutive tiles mostly share the output column block
+// (tiles are numbered m-fastest) and per-column partial sums can stay in registers.
+struct TileRange {
+  int begin, end, step;
+};
+__device__ __forceinline__ TileRange tile_range(const GemmArgs& a, int id, int n, int num_tiles) {
+  if (a.chunked) {
+    return {static_cast<int>((static_cast<long long>(id) * num_tiles) / n),
+            static_cast<int>((static_cast<long long>(id + 1) * num_tiles) / n), 1};
+  }
+  return {id, num_tiles, n};
+}
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -110,9 +127,11 @@ __device__ __forceinline__ void epi_copy_out(const uint8_t* stg, int lane, void*
 
 // One staged round: `r` holds kCols accumulator columns of this thread's row
 // (row0 + lane), starting at output column col0.
+// `cs` (kEpiDGelu with column sums): this lane's running sums of the 8 output columns it
+// stores in this round (rows differ between lanes; flushed by gemm_colsum_flush).
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* stg, int lane, int row0, int col0,
-                                                    const uint32_t* r) {
+                                                    const uint32_t* r, float* cs = nullptr) {
   using T = EpiTraits<EPI>;
   constexpr int NC = T::kCols;
   float v[NC];
@@ -191,9 +210,6 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
     }
     epi_stage_row<true>(stg, lane, v);
     __syncwarp();
-    float cs[8];  // column sums of the rounded outputs (bias gradient of the producing layer)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) cs[e] = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rr = 4 * i + (lane >> 3);
@@ -207,24 +223,14 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
           const float2 g = unpack_bf16x2(wa[e]);
           const float2 pre = unpack_bf16x2(xa[e]);
           o[e] = pack_bf16x2(g.x * gelu_erf_grad(pre.x), g.y * gelu_erf_grad(pre.y));
-          const float2 r = unpack_bf16x2(o[e]);
-          cs[2 * e] += r.x;
-          cs[2 * e + 1] += r.y;
+          if (cs != nullptr) {
+            const float2 r = unpack_bf16x2(o[e]);
+            cs[2 * e] += r.x;
+            cs[2 * e + 1] += r.y;
+          }
         }
         *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
             make_uint4(o[0], o[1], o[2], o[3]);
-      }
-    }
-    if (a.colsum != nullptr) {  // warp-uniform
-      // lanes u, u+8, u+16, u+24 hold the same 8 columns for different rows
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 8);
-        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 16);
-      }
-      if (lane < 8 && col < a.N) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) atomicAdd(a.colsum + col + e, cs[e]);
       }
     }
   } else if constexpr (EPI == kEpiAtomicF32) {
@@ -259,6 +265,68 @@ __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* s
     tmem_wait_ld();
     gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r);
   }
+}
+
+// GELU-backward epilogue with bias-gradient column sums: as above, but each lane adds the
+// columns it stores into cs[round][8], kept in registers across the consecutive tiles of
+// one output column block.  One flush (shuffle reduction + one atomic per column and warp)
+// per column block replaces an atomic per column, warp and round of every tile: with 32
+// row tiles per column block sharing 256 addresses, those atomics serialised in L2 and
+// cost more than the GEMM itself (76 -> 122 us at 8192 x 4096 x 1024).
+template <int HALF_COLS>
+__device__ __forceinline__ void gemm_epilogue_warp_dgelu_cs(const GemmArgs& a, uint8_t* stg, int lane,
+                                                            uint32_t taddr, int row0, int col0,
+                                                            float (&cs)[HALF_COLS / 64][8]) {
+#pragma unroll
+  for (int rd = 0; rd < HALF_COLS / 64; ++rd) {
+    if (col0 + rd * 64 >= a.N) break;  // warp-uniform
+    uint32_t r[64];
+    tmem_ld32(taddr + rd * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    tmem_ld32(taddr + rd * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    tmem_wait_ld();
+    gemm_epilogue_round<kEpiDGelu>(a, stg, lane, row0, col0 + rd * 64, r, cs[rd]);
+  }
+}
+
+// Adds the column sums held in cs (columns col0 .. col0 + HALF_COLS of this warp's rows)
+// to a.colsum and clears them.  Lanes u, u + 8, u + 16, u + 24 hold the same 8 columns.
+template <int HALF_COLS>
+__device__ __forceinline__ void gemm_colsum_flush(const GemmArgs& a, int lane, int col0,
+                                                  float (&cs)[HALF_COLS / 64][8]) {
+#pragma unroll
+  for (int rd = 0; rd < HALF_COLS / 64; ++rd) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      cs[rd][e] += __shfl_xor_sync(0xffffffffu, cs[rd][e], 8);
+      cs[rd][e] += __shfl_xor_sync(0xffffffffu, cs[rd][e], 16);
+    }
+    const int col = col0 + rd * 64 + (lane & 7) * 8;
+    if (lane < 8 && col < a.N) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(a.colsum + col + e, cs[rd][e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cs[rd][e] = 0.f;
+  }
+}
+
+// One warp's share of one output tile.  With kEpiDGelu and column sums, `cs` carries the
+// column sums of column block `cs_tn` across tiles; a new column block flushes them first.
+template <int EPI, int HALF_COLS>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
+                                                   int row0, int col0, int tn, float (&cs)[HALF_COLS / 64][8],
+                                                   int& cs_tn) {
+  if constexpr (EPI == kEpiDGelu) {
+    if (a.colsum != nullptr) {  // warp-uniform
+      if (tn != cs_tn) {
+        if (cs_tn >= 0) gemm_colsum_flush<HALF_COLS>(a, lane, col0 + (cs_tn - tn) * 2 * HALF_COLS, cs);
+        cs_tn = tn;
+      }
+      gemm_epilogue_warp_dgelu_cs<HALF_COLS>(a, stg, lane, taddr, row0, col0, cs);
+      return;
+    }
+  }
+  gemm_epilogue_warp<EPI, HALF_COLS>(a, stg, lane, taddr, row0, col0);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -319,6 +387,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
+  const TileRange trange = tile_range(args, blockIdx.x, gridDim.x, num_tiles);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -326,7 +395,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, issued_parity = 0;  // per-stage bits, for the drain on abort
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      for (int t = trange.begin; t < trange.end; t += trange.step) {
         const int tm = t % args.tiles_m;
         const int rest = t / args.tiles_m;
         const int tn = rest % args.tiles_n;
@@ -382,7 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t acc_phase = 0;
       const uint32_t a_base = smem_u32(sA);
       const uint32_t b_base = smem_u32(sB);
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      for (int t = trange.begin; t < trange.end; t += trange.step) {
         const int rest = t / args.tiles_m;
         const int ts = rest / args.tiles_n;
         const int kb0 = ts * args.kb_per_split;
@@ -431,15 +500,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = ew >> 2;   // column half handled by this warp
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    float cs[BN / 128][8] = {};  // kEpiDGelu column sums of the current column block
+    int cs_tn = -1;
+    for (int t = trange.begin; t < trange.end; t += trange.step) {
       const int tm = t % args.tiles_m;
       const int tn = (t / args.tiles_m) % args.tiles_n;
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
-      gemm_epilogue_warp<EPI, BN / 2>(
-          args, sEpi + ew * kEpiStageBytes, lane,
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2)),
-          tm * BM + q * 32, tn * BN + half * (BN / 2));
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2));
+      gemm_epilogue_tile<EPI, BN / 2>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tm * BM + q * 32,
+                                      tn * BN + half * (BN / 2), tn, cs, cs_tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -447,6 +518,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    if constexpr (EPI == kEpiDGelu) {
+      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / 2>(args, lane, cs_tn * BN + half * (BN / 2), cs);
     }
   }
 
@@ -532,6 +606,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
+  const TileRange trange = tile_range(args, cluster_id, num_clusters, num_tiles);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -540,7 +615,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0, issued_parity = 0;
       const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
-      for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      for (int t = trange.begin; t < trange.end; t += trange.step) {
         const int tm = t % args.tiles_m;
         const int rest = t / args.tiles_m;
         const int tn = rest % args.tiles_n;
@@ -603,7 +678,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t acc_phase = 0;
       const uint32_t a_base = smem_u32(sA);
       const uint32_t b_base = smem_u32(sB);
-      for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      for (int t = trange.begin; t < trange.end; t += trange.step) {
         const int rest = t / args.tiles_m;
         const int ts = rest / args.tiles_n;
         const int kb0 = ts * args.kb_per_split;
@@ -655,15 +730,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+    float cs[BN / 128][8] = {};  // kEpiDGelu column sums of the current column block
+    int cs_tn = -1;
+    for (int t = trange.begin; t < trange.end; t += trange.step) {
       const int tm = t % args.tiles_m;
       const int tn = (t / args.tiles_m) % args.tiles_n;
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
-      gemm_epilogue_warp<EPI, BN / 2>(
-          args, sEpi + ew * kEpiStageBytes, lane,
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2)),
-          tm * 2 * BM + crank * BM + q * 32, tn * BN + half * (BN / 2));
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2));
+      gemm_epilogue_tile<EPI, BN / 2>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
+                                      tm * 2 * BM + crank * BM + q * 32, tn * BN + half * (BN / 2), tn, cs, cs_tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
@@ -671,6 +748,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    if constexpr (EPI == kEpiDGelu) {
+      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / 2>(args, lane, cs_tn * BN + half * (BN / 2), cs);
     }
   }
 
@@ -875,6 +955,13 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
     REVPP_CHECK(colsum->is_contiguous() && colsum->numel() >= N, "colsum must hold N floats");
     args.colsum = colsum->data_ptr<float>();
   }
+  // Contiguous tile runs keep the column-sum partials of the GELU-backward epilogue in
+  // registers; REVPP_GEMM_CHUNKED=1 / 0 forces the order for every GEMM (measurements).
+  static const int chunk_env = [] {
+    const char* e = std::getenv("REVPP_GEMM_CHUNKED");
+    return e == nullptr ? -1 : std::atoi(e);
+  }();
+  args.chunked = chunk_env >= 0 ? (chunk_env != 0) : (args.colsum != nullptr);
   args.status = status_device_ptr();
 
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

@@ -156,18 +156,22 @@ __global__ void __launch_bounds__(kLnWarps * 32, VPL <= 8 ? 2 : 1)
     }
   }
   __syncthreads();
-  const float* sa = reinterpret_cast<const float*>(s_acc4);
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float tg = 0.f, tb = 0.f, tc = 0.f;
+  // one 16-byte vector atomic per 4 columns and block (a scalar atomic per column put
+  // four times as many same-line operations in L2's queue)
+  for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+    float4 tg = make_float4(0.f, 0.f, 0.f, 0.f), tb = tg, tc = tg;
 #pragma unroll
     for (int w = 0; w < kLnWarps; ++w) {
-      tg += sa[(w * 3 + 0) * H + c];
-      tb += sa[(w * 3 + 1) * H + c];
-      tc += sa[(w * 3 + 2) * H + c];
+      const float4 g = s_acc4[(w * 3 + 0) * (H / 4) + c4];
+      const float4 b = s_acc4[(w * 3 + 1) * (H / 4) + c4];
+      const float4 c = s_acc4[(w * 3 + 2) * (H / 4) + c4];
+      tg.x += g.x; tg.y += g.y; tg.z += g.z; tg.w += g.w;
+      tb.x += b.x; tb.y += b.y; tb.z += b.z; tb.w += b.w;
+      tc.x += c.x; tc.y += c.y; tc.z += c.z; tc.w += c.w;
     }
-    if (dgamma) atomicAdd(dgamma + c, tg);
-    if (dbeta) atomicAdd(dbeta + c, tb);
-    if (colsum) atomicAdd(colsum + c, tc);
+    if (dgamma) atomicAdd(reinterpret_cast<float4*>(dgamma) + c4, tg);
+    if (dbeta) atomicAdd(reinterpret_cast<float4*>(dbeta) + c4, tb);
+    if (colsum) atomicAdd(reinterpret_cast<float4*>(colsum) + c4, tc);
   }
 }
 
@@ -214,10 +218,7 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < 3; ++k) {
       acc.x += red[k][tx].x; acc.y += red[k][tx].y; acc.z += red[k][tx].z; acc.w += red[k][tx].w;
     }
-    atomicAdd(colsum + 4 * c4 + 0, acc.x);
-    atomicAdd(colsum + 4 * c4 + 1, acc.y);
-    atomicAdd(colsum + 4 * c4 + 2, acc.z);
-    atomicAdd(colsum + 4 * c4 + 3, acc.w);
+    atomicAdd(reinterpret_cast<float4*>(colsum) + c4, acc);
   }
 }
 
@@ -291,6 +292,12 @@ void layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch:
   if (M == 0) return;
   c10::cuda::CUDAGuard guard(x.device());
   const bool dy_bf16 = dy.scalar_type() == at::kBFloat16;
+  for (const auto* t : {&dgamma, &dbeta, &colsum}) {  // the column sums use 16-byte vector atomics
+    if (t->has_value() && (*t)->defined()) {
+      REVPP_CHECK((*t)->numel() >= H && (reinterpret_cast<uintptr_t>((*t)->data_ptr()) & 15) == 0,
+                  "LayerNorm backward gradient sums need 16-byte aligned fp32 buffers of H elements");
+    }
+  }
   float* dxf = opt_f32(dx_f32);
   __nv_bfloat16* dxb = nullptr;
   long long lddx = H;
@@ -347,6 +354,8 @@ void cast_colsum(const torch::Tensor& in, const c10::optional<torch::Tensor>& ou
     ldo = out->stride(0);
   }
   float* cs = opt_f32(colsum);
+  REVPP_CHECK(cs == nullptr || (reinterpret_cast<uintptr_t>(cs) & 15) == 0,
+              "cast_colsum: colsum must be 16-byte aligned (vector atomics)");
   dim3 grid((M + kColTileRows - 1) / kColTileRows, (N / 4 + 63) / 64);
   if (in.scalar_type() == at::kBFloat16) {
     cast_colsum_kernel<true><<<grid, 256, 0, cur_stream()>>>(in.data_ptr(), in.stride(0), M, N, nullptr, 0, cs);

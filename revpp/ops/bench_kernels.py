@@ -5,6 +5,7 @@
     python -m revpp.ops.bench_kernels attn-bwd --B 16 --S 512 --heads 16
     python -m revpp.ops.bench_kernels layernorm --M 16384 --H 1024
     python -m revpp.ops.bench_kernels adamw --n 335000000
+    python -m revpp.ops.bench_kernels suite --B 16 --S 512 --heads 16   # every kernel of one layer
 
 Each run warms up, then times ``--iters`` launches between CUDA events and prints one JSON
 line with the time per launch and the achieved TFLOP/s or GB/s.  ``--iters 1 --warmup 1``
@@ -49,19 +50,22 @@ def bench_gemm(a, C):
         B = (torch.randn(K, N, device=dev) * 0.05).to(torch.bfloat16)
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         aux = torch.randn(M, N, device=dev).to(torch.bfloat16) if epi == 4 else None
-        fn = lambda: C.gemm_tc(A, False, B, True, M, N, K, epi, out, aux=aux, variant=a.variant)  # noqa: E731
+        cs = torch.zeros(N, device=dev) if (epi == 4 and a.colsum) else None
+        fn = lambda: C.gemm_tc(A, False, B, True, M, N, K, epi, out, aux=aux, variant=a.variant,  # noqa: E731
+                               colsum=cs)
     else:
         A = torch.randn(M, K, device=dev).to(torch.bfloat16)
         B = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
         bias = torch.zeros(N, device=dev, dtype=torch.bfloat16)
         f32 = epi in (2, 5)
         out = torch.empty(M, N, device=dev, dtype=torch.float32 if f32 else torch.bfloat16)
-        aux = torch.empty(M, N, device=dev, dtype=torch.bfloat16) if epi == 1 else None
+        aux = torch.empty(M, N, device=dev, dtype=torch.bfloat16) if (epi == 1 and not a.no_aux_out) else None
         resid = torch.randn(M, N, device=dev) if epi == 2 else None
         fn = lambda: C.gemm_tc(A, False, B, False, M, N, K, epi, out, bias=bias, aux_out=aux,  # noqa: E731
                                resid=resid, variant=a.variant)
     ms = _time(fn, a.warmup, a.iters)
     return {"op": "gemm", "layout": a.layout, "epi": a.epi, "variant": a.variant, "M": M, "N": N, "K": K,
+            "colsum": bool(a.colsum), "aux_out": a.epi == "gelu" and not a.no_aux_out,
             "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9}
 
 
@@ -83,7 +87,11 @@ def bench_attn(a, C, backward: bool):
     dq = torch.empty(B * S, H, device="cuda")
     D = torch.empty(B, heads, S, device="cuda")
     bwd = C.attn_bwd_tc if a.impl == "tc" else C.attn_bwd
-    ms = _time(lambda: bwd(qkv, out, dout, lse, dqkv, dq, D, B, S, heads), a.warmup, a.iters)
+    if a.impl == "tc":  # with the fused q/k/v bias-gradient column sums, as in training
+        cs = torch.zeros(3 * H, device="cuda")
+        ms = _time(lambda: bwd(qkv, out, dout, lse, dqkv, dq, D, B, S, heads, colsum=cs), a.warmup, a.iters)
+    else:
+        ms = _time(lambda: bwd(qkv, out, dout, lse, dqkv, dq, D, B, S, heads), a.warmup, a.iters)
     return {"op": "attn-bwd", "impl": a.impl, "B": B, "S": S, "heads": heads, "ms": ms,
             "tflops": 2.5 * flops / ms / 1e9}
 
@@ -133,9 +141,37 @@ def bench_adamw(a, C):
     return {"op": "adamw", "n": n, "ms": ms, "gbs": bytes_ / ms / 1e6}
 
 
+def layer_suite(a):
+    """Argument lists of every kernel of one reversible encoder layer for one micro-batch
+    (tokens T = B*S, hidden H, FFN 4H): forward / reconstruction GEMMs with their
+    epilogues, input-gradient and weight-gradient GEMMs, attention forward / backward,
+    LayerNorm."""
+    T, H, I = a.B * a.S, a.heads * 64, 4 * a.heads * 64
+    g = ["gemm", "--M", str(T)]
+    return [
+        g + ["--N", str(3 * H), "--K", str(H), "--epi", "bf16"],                      # QKV
+        g + ["--N", str(H), "--K", str(H), "--epi", "resid"],                         # out-proj + residual
+        g + ["--N", str(I), "--K", str(H), "--epi", "gelu", "--no-aux-out"],          # FFN1 + GELU
+        g + ["--N", str(I), "--K", str(H), "--epi", "gelu"],                          # FFN1 + GELU, saves u
+        g + ["--N", str(H), "--K", str(I), "--epi", "resid"],                         # FFN2 + residual
+        g + ["--N", str(I), "--K", str(H), "--layout", "dgrad", "--epi", "dgelu"],    # du
+        g + ["--N", str(I), "--K", str(H), "--layout", "dgrad", "--epi", "dgelu", "--colsum"],
+        g + ["--N", str(H), "--K", str(I), "--layout", "dgrad", "--epi", "bf16"],     # d LN2 out
+        g + ["--N", str(H), "--K", str(H), "--layout", "dgrad", "--epi", "bf16"],     # d attn out
+        g + ["--N", str(H), "--K", str(3 * H), "--layout", "dgrad", "--epi", "bf16"],  # d LN1 out
+        ["gemm", "--M", str(H), "--N", str(I), "--K", str(T), "--layout", "wgrad", "--epi", "atomic"],   # dW2
+        ["gemm", "--M", str(I), "--N", str(H), "--K", str(T), "--layout", "wgrad", "--epi", "atomic"],   # dW1
+        ["gemm", "--M", str(H), "--N", str(H), "--K", str(T), "--layout", "wgrad", "--epi", "atomic"],   # dWo
+        ["gemm", "--M", str(3 * H), "--N", str(H), "--K", str(T), "--layout", "wgrad", "--epi", "atomic"],  # dWqkv
+        ["attn-fwd", "--B", str(a.B), "--S", str(a.S), "--heads", str(a.heads)],
+        ["attn-bwd", "--B", str(a.B), "--S", str(a.S), "--heads", str(a.heads)],
+        ["layernorm", "--M", str(T), "--H", str(H)],
+    ]
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "layernorm", "adamw"])
+    p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "layernorm", "adamw", "suite"])
     p.add_argument("--M", type=int, default=16384)
     p.add_argument("--N", type=int, default=4096)
     p.add_argument("--K", type=int, default=1024)
@@ -143,6 +179,8 @@ def main(argv=None):
     p.add_argument("--epi", choices=list(EPIS), default="bf16")
     p.add_argument("--layout", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     p.add_argument("--variant", type=int, default=0)
+    p.add_argument("--colsum", action="store_true", help="dgelu: fused bias-gradient column sums")
+    p.add_argument("--no-aux-out", action="store_true", help="gelu: do not write the pre-activation")
     p.add_argument("--B", type=int, default=16)
     p.add_argument("--S", type=int, default=512)
     p.add_argument("--heads", type=int, default=16)
@@ -154,6 +192,11 @@ def main(argv=None):
     from revpp.ops import ext
 
     C = ext()
+    if a.op == "suite":
+        extra = ["--warmup", str(a.warmup), "--iters", str(a.iters)]
+        for args in layer_suite(a):
+            main(args + extra)
+        return
     if a.op == "gemm":
         r = bench_gemm(a, C)
     elif a.op == "attn-fwd":

@@ -105,6 +105,27 @@ def test_dgelu(M, N, K, variant):
     assert (cs.double() - ref_cs).abs().max().item() <= 1e-4 * (1 + ref_cs.abs().max().item())
 
 
+@pytest.mark.parametrize("variant", [1, 2])
+def test_dgelu_colsum_many_tiles(variant):
+    """Column sums over many tiles per CTA: contiguous tile runs cross column blocks, so
+    the register-held partial sums are flushed mid-kernel as well as at the end."""
+    C = _C()
+    M, N, K = 8192, 4096, 1024
+    a, w = _rand(M, K), _rand(K, N, scale=0.05)
+    u = _rand(M, N)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cs = torch.full((N,), -1.0, device="cuda")
+    C.gemm_tc(a, False, w, True, M, N, K, EPI_DGELU, out, aux=u, variant=variant, colsum=cs)
+    torch.cuda.synchronize()
+    ref_cs = out.double().sum(0) - 1.0
+    assert (cs.double() - ref_cs).abs().max().item() <= 1e-4 * (1 + ref_cs.abs().max().item())
+    ud = u.double()[:256]
+    dg = 0.5 * (1 + torch.erf(ud / math.sqrt(2))) + ud * torch.exp(-0.5 * ud * ud) / math.sqrt(2 * math.pi)
+    dh = (a[:256].double() @ w.double()).to(torch.bfloat16).double()
+    _close(out[:256], dh * dg, 2e-2)
+    assert C.status_read_and_clear() == 0
+
+
 WGRAD_SHAPES = [(128, 256, 64), (256, 512, 256), (96, 160, 197 * 3), (1024, 1024, 1000), (3072, 1024, 4096)]
 
 
