@@ -6,14 +6,19 @@
 //   warp 0     : TMA producer - Q once, then K_j / V_j into a 3-deep ring (no multicast)
 //   warp 1     : TMEM allocator and MMA issuer (one thread):
 //                  S_j  = Q K_j^T   (M 128, N 64, K 64)  -> TMEM S[j % 2]
-//                  PV_j = P_j V_j   (M 128, N 64, K 64)  -> TMEM PV[j % 2]
+//                  O   += P_j V_j   (M 128, N 64, K 64)  -> TMEM O (accumulated over j)
 //                S_{j+1} is issued before waiting for P_j, so the tensor core works on the
 //                next scores while the softmax warps handle the current ones.
-//   warps 2-5  : softmax, one thread per query row: S row from TMEM, online max / sum in
-//                fp32 (hardware exp2 with the 1/sqrt(d) * log2(e) scale folded into one FMA
-//                after the row max), P_j as bf16 into a
-//                128-byte-swizzled smem tile (the MMA's A operand), and O accumulated in
-//                registers: O = O * alpha_{j-1} + PV_{j-1}.
+//   warps 2-5  : softmax, one thread per query row: S row from TMEM, P_j = exp2(S * scale
+//                - m) as bf16 into a 128-byte-swizzled smem tile (the MMA's A operand),
+//                running row sum l in fp32.
+// The output accumulates in TMEM with a reference maximum m that is raised only when a
+// row's new maximum exceeds it by more than 8 (log2 units): P then stays <= 256, and the
+// rescale (O *= 2^(m_old - m_new) through tcgen05.ld / st, after the previous P V has
+// landed) is rare, so the per-tile work of a softmax thread is one TMEM load, the max,
+// the exponentials and the P store - no per-tile output correction.  Softmax is
+// invariant to the reference maximum, so the result equals the exact-max formulation up
+// to rounding.
 // Shared memory ~97 KB and 256 TMEM columns, so two CTAs share an SM.
 #include "common.cuh"
 #include "host.h"
@@ -29,7 +34,9 @@ constexpr int kThreads = 192;
 constexpr uint32_t kQBytes = kQ * kDh * 2;     // 16 KB
 constexpr uint32_t kKVBytes = kKV * kDh * 2;   // 8 KB (one of K or V)
 constexpr uint32_t kPBytes = kQ * kKV * 2;     // 16 KB
-constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + PV[2] (64 each)
+constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + O (64)
+constexpr uint32_t kTmemO = 128;
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8
 constexpr uint32_t kIdescS = idesc_bf16(kQ, kKV, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16(kQ, kDh, false, true);
 
@@ -66,9 +73,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_empty = s_full + 2;           // [2]
   uint64_t* p_full = s_empty + 2;           // [2]
   uint64_t* p_empty = p_full + 2;           // [2]
-  uint64_t* pv_full = p_empty + 2;          // [2]
-  uint64_t* pv_empty = pv_full + 2;         // [2]
-  uint64_t* drain = pv_empty + 2;
+  uint64_t* pv_done = p_empty + 2;          // completes once per P V (in order)
+  uint64_t* drain = pv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -91,9 +97,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
-      mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_empty[i], 4);
     }
+    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -151,18 +156,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       auto issue_pv = [&](int j) -> bool {
         const int pb = j & 1;
         const uint32_t par = (j >> 1) & 1;
+        // P_j is in smem, and any rescale of O by the softmax threads has been stored
         if (!mbar_wait(&p_full[pb], par, args.status, abort_flag)) return false;
-        if (!mbar_wait(&pv_empty[pb], par ^ 1u, args.status, abort_flag)) return false;
         tc_fence_after();
         const int st = j % kStages;
-        const uint32_t d = tmem + 128 + pb * kDh;
 #pragma unroll
         for (int k = 0; k < kKV / 16; ++k) {
           const uint64_t ad = sdesc_sw128(p_addr + pb * kPBytes + k * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + st * kKVBytes + k * 2048, 8192, 1024);
-          umma_bf16_ss(d, ad, bd, kIdescPV, k > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + kTmemO, ad, bd, kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&pv_full[pb]);
+        umma_commit(pv_done);
         umma_commit(&p_empty[pb]);
         umma_commit(&kv_empty[st]);
         return true;
@@ -199,10 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = quarter * 32 + lane;           // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     uint8_t* p_base = smem + SmemLayout::p;
-    float o[kDh];
-#pragma unroll
-    for (int i = 0; i < kDh; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    float m = -INFINITY, l = 0.f;
     const float sl2 = args.scale_log2;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -230,80 +231,91 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kKV; ++c)
           if (kbase + c >= S) sv[c] = -INFINITY;
       }
-      float rmx = sv[0];
+      // row max as 8 independent chains
+      float pm[8];
 #pragma unroll
-      for (int c = 1; c < kKV; ++c) rmx = fmaxf(rmx, sv[c]);
-      const float mx = fmaxf(m, rmx * sl2);
-      const float alpha = ex2_approx(m - mx);
-      float rs = 0.f;
-      l *= alpha;
-      m = mx;
+      for (int i = 0; i < 8; ++i) pm[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < kKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], sv[c]);
+      const float tmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                              fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
+      if (j == 0) {
+        m = tmx;  // key 0 is always valid, so m is finite
+      } else if (__any_sync(0xffffffffu, tmx > m + kRescaleThreshold)) {
+        // raise the reference maximum of this warp's rows; O holds P_0..P_{j-1} V once
+        // the previous P V has completed
+        const float mn = fmaxf(m, tmx);
+        const float alpha = ex2_approx(m - mn);
+        m = mn;
+        l *= alpha;
+        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, args.status, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + kTmemO + 32 * hh, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_off + kTmemO + 32 * hh, o);
+        }
+        tmem_wait_st();
+      }
       // P_j -> smem (A operand of P V, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7))
       if (!mbar_wait(&p_empty[sb], par ^ 1u, args.status, abort_flag)) {
         ok = false;
         break;
       }
       uint8_t* prow = p_base + sb * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+      float rsp[8];  // row-sum partials, one per 16-byte unit
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t w[4];
+        float ps = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(sv[8 * c + 2 * e], sl2, -mx));
-          const float p1 = ex2_approx(fmaf(sv[8 * c + 2 * e + 1], sl2, -mx));
-          rs += p0 + p1;
+          const float p0 = ex2_approx(fmaf(sv[8 * c + 2 * e], sl2, -m));
+          const float p1 = ex2_approx(fmaf(sv[8 * c + 2 * e + 1], sl2, -m));
+          ps += p0 + p1;
           w[e] = pack_bf16x2(p0, p1);
         }
+        rsp[c] = ps;
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l += rs;
+      l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
-      // fold in PV_{j-1}
-      if (j >= 1) {
-        const int pb = (j - 1) & 1;
-        if (!mbar_wait(&pv_full[pb], ((j - 1) >> 1) & 1, args.status, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t pv[2][32];
-        tmem_ld32(tmem + lane_off + 128 + pb * kDh, pv[0]);
-        tmem_ld32(tmem + lane_off + 128 + pb * kDh + 32, pv[1]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pv_empty[pb]);
-#pragma unroll
-        for (int i = 0; i < kDh; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(pv[i >> 5][i & 31]);
-      }
-      alpha_prev = alpha;
     }
-    if (ok && nkv >= 1) {
-      const int pb = (nkv - 1) & 1;
-      if (mbar_wait(&pv_full[pb], ((nkv - 1) >> 1) & 1, args.status, abort_flag)) {
-        tc_fence_after();
-        uint32_t pv[2][32];
-        tmem_ld32(tmem + lane_off + 128 + pb * kDh, pv[0]);
-        tmem_ld32(tmem + lane_off + 128 + pb * kDh + 32, pv[1]);
+    // the last P V completes the output
+    bool fin = ok && nkv >= 1;
+    if (fin) fin = mbar_wait(pv_done, (nkv - 1) & 1, args.status, abort_flag);
+    if (__all_sync(0xffffffffu, fin)) {
+      tc_fence_after();
+      const int q = q0 + r;
+      const float inv = 1.f / l;
+      uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_off + kTmemO + 32 * hh, o);
         tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < kDh; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(pv[i >> 5][i & 31]);
-        const int q = q0 + r;
         if (q < S) {
-          const float inv = 1.f / l;
-          uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            dst[c] = make_uint4(pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv),
-                                pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
-                                pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
-                                pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+          for (int c = 0; c < 4; ++c) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * c + e]) * inv;
+            dst[4 * hh + c] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                                         pack_bf16x2(f[6], f[7]));
           }
-          args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (m + log2f(l)) * 0.69314718055994531f;
         }
       }
+      if (q < S) args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (m + log2f(l)) * 0.69314718055994531f;
     }
   }
   tc_fence_before();

@@ -11,8 +11,9 @@
 // Warp roles (320 threads):
 //   warp 0      : TMA producer (one thread), STAGES-deep smem ring, no multicast
 //   warp 1      : TMEM allocator + MMA issuer (one thread), tcgen05.mma 128xBNx16
-//   warps 2..9  : epilogue; TMEM -> registers (tcgen05.ld) -> fused op -> per-warp smem
-//                 staging tile -> row-contiguous global stores
+//   warps 2..9  : epilogue, one (TMEM lane quarter, column half) each; TMEM ->
+//                 registers (tcgen05.ld) -> fused op -> per-warp smem staging tile ->
+//                 row-contiguous global stores
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of
 // tile i overlaps the main loop of tile i+1.
 //
@@ -68,7 +69,11 @@ __device__ __forceinline__ TileRange tile_range(const GemmArgs& a, int id, int n
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
+// 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 2) / 4 of
+// the tile.  (16 warps, each a column quarter, measured no faster: their 64 KB of staging
+// tiles cost an operand stage, and 18 warps cap the registers at 96 per thread.)
 constexpr int kGemmEpiWarps = 8;
+constexpr int kGemmColGroups = kGemmEpiWarps / 4;
 constexpr int kGemmThreads = 64 + kGemmEpiWarps * 32;
 
 // ------------------------------------------------------------------ epilogue
@@ -158,18 +163,28 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
     __syncwarp();
     epi_copy_out<T::kBf16Stage ? 2 : 4>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
   } else if constexpr (EPI == kEpiGelu) {
-    float h[NC];
+    // unit by unit, so the GELU values never coexist with all 64 accumulators; the bf16
+    // pre-activations stay packed for the optional aux_out copy
+    uint32_t pre[NC / 2];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) {
-      v[j] = bf16r(v[j]);
-      h[j] = gelu_erf(v[j]);
+    for (int uu = 0; uu < NC / 8; ++uu) {
+      uint32_t hw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x0 = bf16r(v[8 * uu + 2 * e]), x1 = bf16r(v[8 * uu + 2 * e + 1]);
+        pre[4 * uu + e] = pack_bf16x2(x0, x1);
+        hw[e] = pack_bf16x2(gelu_erf(x0), gelu_erf(x1));
+      }
+      *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, uu)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
-    epi_stage_row<true>(stg, lane, h);
     __syncwarp();
     epi_copy_out<2>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
     if (a.aux_out != nullptr) {
       __syncwarp();
-      epi_stage_row<true>(stg, lane, v);
+#pragma unroll
+      for (int uu = 0; uu < NC / 8; ++uu)
+        *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, uu)) =
+            make_uint4(pre[4 * uu], pre[4 * uu + 1], pre[4 * uu + 2], pre[4 * uu + 3]);
       __syncwarp();
       epi_copy_out<2>(stg, lane, a.aux_out, a.ld_aux, row0, col0, a.M, a.N);
     }
@@ -249,15 +264,15 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
   __syncwarp();  // the staging tile is rewritten by the next round
 }
 
-// The epilogue of one warp for one tile: HALF_COLS accumulator columns starting at TMEM
+// The epilogue of one warp for one tile: WARP_COLS accumulator columns starting at TMEM
 // address `taddr` (lane quarter and column already applied), output rows row0..row0+31,
 // output columns from col0.
-template <int EPI, int HALF_COLS>
+template <int EPI, int WARP_COLS>
 __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
                                                    int row0, int col0) {
   constexpr int RC = EpiTraits<EPI>::kCols;
 #pragma unroll 1
-  for (int c = 0; c < HALF_COLS; c += RC) {
+  for (int c = 0; c < WARP_COLS; c += RC) {
     if (col0 + c >= a.N) break;  // warp-uniform
     uint32_t r[RC];
     tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -273,12 +288,12 @@ __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* s
 // per column block replaces an atomic per column, warp and round of every tile: with 32
 // row tiles per column block sharing 256 addresses, those atomics serialised in L2 and
 // cost more than the GEMM itself (76 -> 122 us at 8192 x 4096 x 1024).
-template <int HALF_COLS>
+template <int WARP_COLS>
 __device__ __forceinline__ void gemm_epilogue_warp_dgelu_cs(const GemmArgs& a, uint8_t* stg, int lane,
                                                             uint32_t taddr, int row0, int col0,
-                                                            float (&cs)[HALF_COLS / 64][8]) {
+                                                            float (&cs)[WARP_COLS / 64][8]) {
 #pragma unroll
-  for (int rd = 0; rd < HALF_COLS / 64; ++rd) {
+  for (int rd = 0; rd < WARP_COLS / 64; ++rd) {
     if (col0 + rd * 64 >= a.N) break;  // warp-uniform
     uint32_t r[64];
     tmem_ld32(taddr + rd * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -288,13 +303,13 @@ __device__ __forceinline__ void gemm_epilogue_warp_dgelu_cs(const GemmArgs& a, u
   }
 }
 
-// Adds the column sums held in cs (columns col0 .. col0 + HALF_COLS of this warp's rows)
+// Adds the column sums held in cs (columns col0 .. col0 + WARP_COLS of this warp's rows)
 // to a.colsum and clears them.  Lanes u, u + 8, u + 16, u + 24 hold the same 8 columns.
-template <int HALF_COLS>
+template <int WARP_COLS>
 __device__ __forceinline__ void gemm_colsum_flush(const GemmArgs& a, int lane, int col0,
-                                                  float (&cs)[HALF_COLS / 64][8]) {
+                                                  float (&cs)[WARP_COLS / 64][8]) {
 #pragma unroll
-  for (int rd = 0; rd < HALF_COLS / 64; ++rd) {
+  for (int rd = 0; rd < WARP_COLS / 64; ++rd) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       cs[rd][e] += __shfl_xor_sync(0xffffffffu, cs[rd][e], 8);
@@ -312,21 +327,21 @@ __device__ __forceinline__ void gemm_colsum_flush(const GemmArgs& a, int lane, i
 
 // One warp's share of one output tile.  With kEpiDGelu and column sums, `cs` carries the
 // column sums of column block `cs_tn` across tiles; a new column block flushes them first.
-template <int EPI, int HALF_COLS>
+template <int EPI, int WARP_COLS>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
-                                                   int row0, int col0, int tn, float (&cs)[HALF_COLS / 64][8],
+                                                   int row0, int col0, int tn, float (&cs)[WARP_COLS / 64][8],
                                                    int& cs_tn) {
   if constexpr (EPI == kEpiDGelu) {
     if (a.colsum != nullptr) {  // warp-uniform
       if (tn != cs_tn) {
-        if (cs_tn >= 0) gemm_colsum_flush<HALF_COLS>(a, lane, col0 + (cs_tn - tn) * 2 * HALF_COLS, cs);
+        if (cs_tn >= 0) gemm_colsum_flush<WARP_COLS>(a, lane, col0 + (cs_tn - tn) * kGemmColGroups * WARP_COLS, cs);
         cs_tn = tn;
       }
-      gemm_epilogue_warp_dgelu_cs<HALF_COLS>(a, stg, lane, taddr, row0, col0, cs);
+      gemm_epilogue_warp_dgelu_cs<WARP_COLS>(a, stg, lane, taddr, row0, col0, cs);
       return;
     }
   }
-  gemm_epilogue_warp<EPI, HALF_COLS>(a, stg, lane, taddr, row0, col0);
+  gemm_epilogue_warp<EPI, WARP_COLS>(a, stg, lane, taddr, row0, col0);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -497,10 +512,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // -------------------------------------------------------------- epilogue
     const int ew = warp - 2;
     const int q = warp & 3;     // TMEM lane quarter this warp may access
-    const int half = ew >> 2;   // column half handled by this warp
+    const int cg = ew >> 2;     // column half handled by this warp
     int acc = 0;
     uint32_t acc_phase = 0;
-    float cs[BN / 128][8] = {};  // kEpiDGelu column sums of the current column block
+    float cs[BN / kGemmColGroups / 64][8] = {};  // kEpiDGelu column sums of the current column block
     int cs_tn = -1;
     for (int t = trange.begin; t < trange.end; t += trange.step) {
       const int tm = t % args.tiles_m;
@@ -508,9 +523,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2));
-      gemm_epilogue_tile<EPI, BN / 2>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tm * BM + q * 32,
-                                      tn * BN + half * (BN / 2), tn, cs, cs_tn);
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+      gemm_epilogue_tile<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tm * BM + q * 32,
+                                      tn * BN + cg * (BN / kGemmColGroups), tn, cs, cs_tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -520,7 +535,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if constexpr (EPI == kEpiDGelu) {
-      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / 2>(args, lane, cs_tn * BN + half * (BN / 2), cs);
+      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / kGemmColGroups>(args, lane, cs_tn * BN + cg * (BN / kGemmColGroups), cs);
     }
   }
 
@@ -726,11 +741,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // -------------------------------------------------------------- epilogue (both CTAs)
     const int ew = warp - 2;
     const int q = warp & 3;
-    const int half = ew >> 2;
+    const int cg = ew >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    float cs[BN / 128][8] = {};  // kEpiDGelu column sums of the current column block
+    float cs[BN / kGemmColGroups / 64][8] = {};  // kEpiDGelu column sums of the current column block
     int cs_tn = -1;
     for (int t = trange.begin; t < trange.end; t += trange.step) {
       const int tm = t % args.tiles_m;
@@ -738,9 +753,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + half * (BN / 2));
-      gemm_epilogue_tile<EPI, BN / 2>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
-                                      tm * 2 * BM + crank * BM + q * 32, tn * BN + half * (BN / 2), tn, cs, cs_tn);
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+      gemm_epilogue_tile<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
+                                      tm * 2 * BM + crank * BM + q * 32, tn * BN + cg * (BN / kGemmColGroups), tn, cs, cs_tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
@@ -750,7 +765,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if constexpr (EPI == kEpiDGelu) {
-      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / 2>(args, lane, cs_tn * BN + half * (BN / 2), cs);
+      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / kGemmColGroups>(args, lane, cs_tn * BN + cg * (BN / kGemmColGroups), cs);
     }
   }
 
@@ -813,7 +828,7 @@ void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
 
 void dispatch_gemm2(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                     const GemmArgs& args, int grid, cudaStream_t st) {
-  constexpr int ST = 6;
+  constexpr int ST = 6;  // 6 x 32 KB operand stages + 8 x 4 KB epilogue staging tiles
   if (!a_mn && !b_mn) {
     switch (epi) {
       case kEpiBF16: return launch_gemm2_inst<ST, false, false, kEpiBF16>(ta, tb, args, grid, st);
@@ -841,7 +856,7 @@ void dispatch_gemm2(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const 
 //   A MN-major, B MN-major: weight gradients   (atomic f32 accumulate)
 void dispatch_gemm(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                    const GemmArgs& args, int grid, cudaStream_t st) {
-  constexpr int BN = 256, ST = 4;
+  constexpr int BN = 256, ST = 4;  // 4 x 48 KB operand stages + 8 x 4 KB epilogue staging tiles
   if (!a_mn && !b_mn) {
     switch (epi) {
       case kEpiBF16: return launch_gemm_inst<BN, ST, false, false, kEpiBF16>(ta, tb, args, grid, st);

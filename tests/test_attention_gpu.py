@@ -100,3 +100,29 @@ def test_attn_bwd_tcgen05(B, S, heads):
     scale = 1 + g.abs().max().item()
     assert (dqkv.double() - g).abs().max().item() < 3e-2 * scale
     assert (dqkv.double() - dqkv2.double()).abs().max().item() < 3e-2 * scale
+
+
+@pytest.mark.parametrize("B,S,heads", [(1, 512, 2), (2, 577, 1)])
+def test_attn_fwd_tcgen05_rising_scores(B, S, heads):
+    """Scores that grow along the keys: the row maximum rises by far more than the
+    rescale threshold from one 64-key tile to the next, so the kernel's in-TMEM output
+    rescale runs for every row on most tiles."""
+    C = _C()
+    H = heads * 64
+    x = torch.randn(B, S, 3, heads, 64, device="cuda")
+    x[:, :, 0] = x[:, :, 0].abs() * 0.5 + 1.0           # positive queries
+    ramp = torch.linspace(0.0, 6.0, S, device="cuda").view(1, S, 1, 1)
+    x[:, :, 1] = x[:, :, 1].abs() * 0.5 + ramp           # keys growing with position
+    qkv = x.reshape(B * S, 3 * H).to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+    torch.cuda.synchronize()
+    assert C.status_read_and_clear() == 0
+    o_ref, lse_ref = _ref(qkv.double(), B, S, heads)
+    # the scores span more than 8 log2 units between the first and last key tiles
+    s = qkv.double().view(B, S, 3, heads, 64)
+    sc = (s[:, :, 0] * s[:, :, 1]).sum(-1) / 8.0 / math.log(2.0)
+    assert (sc[:, -1] - sc[:, 0]).min().item() > 16.0
+    assert (out.double() - o_ref).abs().max().item() < 2e-2
+    assert ((lse.double() - lse_ref).abs() / lse_ref.abs().clamp(min=1.0)).max().item() < 2e-3
