@@ -366,40 +366,46 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 // the CTA walks the query tiles (128 queries each):
 //   S^T  = K Q_j^T      (M 128 keys, N 128 queries, K 64)   -> TMEM cols [0, 128)
 //   dP^T = V dO_j^T     (same shape)                         -> TMEM cols [128, 256)
-//   softmax warps (one thread per key): P^T = exp(S^T * scale - lse_q),
-//       dS^T = P^T * (dP^T - D_q), both bf16 into 128-byte-swizzled smem tiles
-//   dV  += P^T dO_j     (M 128 keys, N 64, K 128 queries)   -> TMEM cols [256, 320)
+//   softmax warps (one thread per key): P^T = exp(S^T * scale - lse_q) as bf16 pairs into
+//       TMEM cols [448, 512), dS^T = P^T * (dP^T - D_q) as bf16 into a 128-byte-swizzled
+//       smem tile
+//   dV  += P^T dO_j     (M 128 keys, N 64, K 128 queries; A = P^T from TMEM)
+//                                                            -> TMEM cols [256, 320)
 //   dK  += dS^T Q_j     (same)                               -> TMEM cols [320, 384)
 //   dQ_j = dS K         (M 128 queries, N 64, K 128 keys; dS read MN-major from the dS^T
 //                        tile)                               -> TMEM cols [384, 448)
 //   dQ warps (one thread per query) add dQ_j * scale into an fp32 buffer with atomics.
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK dV, 6-9 dQ,
-// 10-13 softmax (queries 64-127).
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK dV, 6-9 dQ
+// and the LSE / D rows of the next query tile (double-buffered in smem, so the softmax
+// warps never wait for one another), 10-13 softmax (queries 64-127).
 // Overlap: as soon as the softmax of tile j has consumed S^T / dP^T, the issuer starts
 // S^T / dP^T of tile j+1 and only then the dV / dK / dQ MMAs of tile j, so the softmax of
-// tile j+1 runs while the tensor core works on tile j.  P^T and dS^T are therefore
-// double-buffered in shared memory; LSE and D rows are fetched one tile ahead.
+// tile j+1 runs while the tensor core works on tile j.  dS^T is therefore double-buffered
+// in shared memory; P^T (one TMEM buffer) is rewritten only after the previous tile's dV
+// MMAs have read it.
 namespace {
 constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
 constexpr int kBwdThreads = 448;
 constexpr uint32_t kTile = 128 * 64 * 2;       // 16 KB: a [128 x 64] bf16 tile
 constexpr uint32_t kSqTile = 2 * kTile;        // 32 KB: a [128 x 128] bf16 tile (2 swizzle chunks)
+constexpr uint32_t kDqStride = 272;  // 256-byte dQ rows padded by 16: row r's chunk k is in bank group (r + k) % 8
 struct BwdSmem {
   static constexpr uint32_t k = 0;
   static constexpr uint32_t v = k + kTile;
   static constexpr uint32_t q = v + kTile;              // 2 buffers
   static constexpr uint32_t dout = q + 2 * kTile;       // 2 buffers
-  static constexpr uint32_t pt = dout + 2 * kTile;      // P^T, 2 buffers
-  static constexpr uint32_t dst = pt + 2 * kSqTile;     // dS^T, 2 buffers
-  static constexpr uint32_t stats = dst + 2 * kSqTile;  // lse*log2e [128], D [128]
-  static constexpr uint32_t bars = stats + 2 * 128 * 4;
+  static constexpr uint32_t dst = dout + 2 * kTile;     // dS^T, 2 buffers
+  static constexpr uint32_t stats = dst + 2 * kSqTile;  // 2 x {lse*log2e [128], D [128]}
+  static constexpr uint32_t dq = stats + 2 * 2 * 128 * 4;  // dQ_j fp32, 128 rows of 64, 272-byte stride
+  static constexpr uint32_t bars = dq + 128 * kDqStride;
   static constexpr uint32_t total = bars + 256;
 };
 static_assert(BwdSmem::total + 1024 <= 232448, "attention backward exceeds the shared-memory limit");
 constexpr uint32_t kIdescSq = idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescKD = idesc_bf16(128, 64, false, true);
 constexpr uint32_t kIdescQD = idesc_bf16(128, 64, true, true);
+constexpr uint32_t kTmemPt = 448;  // P^T as bf16 pairs: 128 queries in 64 columns
 
 }  // namespace
 
@@ -451,8 +457,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* cs_bar = bar + 16;    // the four dK / dV warps' column sums are in shared memory
-  float* s_lse = reinterpret_cast<float*>(smem + BwdSmem::stats);   // [128]
-  float* s_D = s_lse + 128;                                            // [128]
+  uint64_t* pt_free = bar + 17;   // the dV MMAs of a tile have read P^T from TMEM
+  uint64_t* st_full = bar + 18;   // [2] LSE / D rows of a query tile staged
+  uint64_t* st_empty = bar + 20;  // [2] the eight softmax warps are done with them
+  float* s_stats = reinterpret_cast<float*>(smem + BwdSmem::stats);  // [2][256]: lse*log2e, D
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -480,6 +488,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(drain, 1);
     mbar_init(grp_bar, 8);
     mbar_init(cs_bar, 4);
+    mbar_init(pt_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&st_full[i], 4);
+      mbar_init(&st_empty[i], 8);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -532,7 +545,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t a_v = smem_u32(smem + BwdSmem::v);
       const uint32_t a_q = smem_u32(smem + BwdSmem::q);
       const uint32_t a_do = smem_u32(smem + BwdSmem::dout);
-      const uint32_t a_pt = smem_u32(smem + BwdSmem::pt);
       const uint32_t a_ds = smem_u32(smem + BwdSmem::dst);
       // S^T_j = K Q_j^T and dP^T_j = V dO_j^T into TMEM [0, 256)
       auto issue_s = [&](int j) {
@@ -569,14 +581,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a_ptj = a_pt + pb * kSqTile;
         const uint32_t a_dsj = a_ds + pb * kSqTile;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
+          // dV += P^T dO   (A = P^T from TMEM, 16 queries = 8 columns per MMA; B = dO,
+          // MN-major: d contiguous, queries as K rows)
+          umma_bf16_ts(tmem + 256, tmem + kTmemPt + 8 * k, sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024),
+                       kIdescKD, (j > 0 || k > 0));
+        }
+        umma_commit(pt_free);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
           const uint32_t ka = (k >> 2) * kTile + (k & 3) * 32;   // K-major over queries (2 chunks)
-          // dV += P^T dO   (B = dO, MN-major: d contiguous, queries as K rows)
-          umma_bf16_ss(tmem + 256, sdesc_sw128(a_ptj + ka, 16, 1024),
-                       sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
           // dK += dS^T Q
           umma_bf16_ss(tmem + 320, sdesc_sw128(a_dsj + ka, 16, 1024),
                        sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
@@ -605,40 +621,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int grp = warp >= 10 ? 1 : 0;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;      // key row within the tile
-    const int tid = r;                      // 0..127 within this warpgroup
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const bool key_ok = k0 + r < S;
-    const float ln2inv = 1.4426950408889634f;
-    const float4* s_lse4 = reinterpret_cast<const float4*>(s_lse);
-    const float4* s_D4 = reinterpret_cast<const float4*>(s_D);
-    uint8_t* pt_base = smem + BwdSmem::pt;
     uint8_t* ds_base = smem + BwdSmem::dst;
     bool ok = true;
-    uint32_t grp_phase = 0;
-    auto group_sync = [&]() -> bool {  // all eight softmax warps, bounded
-      __syncwarp();
-      if (lane == 0) mbar_arrive(grp_bar);
-      const bool w = mbar_wait(grp_bar, grp_phase, args.status, abort_flag);
-      grp_phase ^= 1u;
-      return w;
-    };
-    // group 0 stages LSE (log2 units; +inf past the sequence end, so P = 0 there), group 1
-    // stages D; both one query tile ahead
-    auto fetch = [&](int q) -> float {
-      if (grp == 0) return q < S ? g_lse[q] * ln2inv : __int_as_float(0x7f800000);
-      return q < S ? g_D[q] : 0.f;
-    };
-    float pre = fetch(tid);
     for (int j = 0; j < nq; ++j) {
       const uint32_t jp = j & 1;
       const uint32_t pb = j & 1;
-      if (!group_sync()) {  // every softmax warp is done with the previous tile's stats
-        ok = false;
-        break;
-      }
-      (grp == 0 ? s_lse : s_D)[tid] = pre;
-      if (j + 1 < nq) pre = fetch((j + 1) * kBQ + tid);
-      if (!group_sync()) {
+      const float4* s_lse4 = reinterpret_cast<const float4*>(s_stats + pb * 256);
+      const float4* s_D4 = s_lse4 + 32;
+      if (!mbar_wait(&st_full[pb], (j >> 1) & 1, args.status, abort_flag)) {
         ok = false;
         break;
       }
@@ -650,10 +642,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
+      // P^T of the previous tile has been read by its dV MMAs (warp-uniform: tcgen05.st
+      // below is a warp-wide instruction)
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pt_free, (j - 1) & 1, args.status, abort_flag))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const int sw = r & 7;
-      // this group's 64 queries are 64-query swizzle chunk `grp` of the P^T / dS^T tiles
-      uint8_t* prow = pt_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
+      // this group's 64 queries are 64-query swizzle chunk `grp` of the dS^T tile
       uint8_t* drow = ds_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
       const float sl2 = args.scale_log2;
 #pragma unroll 1
@@ -686,15 +683,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e) pw[e] = dw[e] = 0u;
         }
-        // 32 queries = 64 bytes = four 16-byte units of the row
+        // P^T: queries 32c .. 32c + 31 are TMEM columns kTmemPt + 16c .. + 15 of this key's lane
+        tmem_st16(tmem + lane_off + kTmemPt + 16 * c, pw);
+        // dS^T: 32 queries = 64 bytes = four 16-byte units of the row
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int u = cc * 4 + t;
           const uint32_t off = (u ^ sw) << 4;
-          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * t], pw[4 * t + 1], pw[4 * t + 2], pw[4 * t + 3]);
           *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st_empty[pb]);  // this warp is done with the tile's LSE / D
+      tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
@@ -735,8 +736,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             cv[2 * e] = key_ok ? r2.x : 0.f;
             cv[2 * e + 1] = key_ok ? r2.y : 0.f;
           }
-          // this warp's 32 keys; the P^T buffers are free once kv_done has fired
-          reinterpret_cast<float*>(smem + BwdSmem::pt)[quarter * 128 + part * 32 + lane] =
+          // this warp's 32 keys; the dS^T buffers are free once kv_done has fired
+          reinterpret_cast<float*>(smem + BwdSmem::dst)[quarter * 128 + part * 32 + lane] =
               warp_column_sums32(cv, lane);
         }
       }
@@ -746,7 +747,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(cs_bar);
         if (quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
-          const float* red = reinterpret_cast<const float*>(smem + BwdSmem::pt);
+          const float* red = reinterpret_cast<const float*>(smem + BwdSmem::dst);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int c = i * 32 + lane;  // 0..63 dK columns, 64..127 dV columns
@@ -761,7 +762,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    // LSE (log2 units; +inf past the sequence end, so P = 0 there) and D of query tile t
+    // into stats buffer t & 1, once the softmax warps are done with tile t - 2
+    auto stage_stats = [&](int t) -> bool {
+      const int sb = t & 1;
+      if (t >= 2 && !mbar_wait(&st_empty[sb], ((t >> 1) & 1) ^ 1u, args.status, abort_flag)) return false;
+      const int q = t * kBQ + r;
+      s_stats[sb * 256 + r] = q < S ? g_lse[q] * 1.4426950408889634f : __int_as_float(0x7f800000);
+      s_stats[sb * 256 + 128 + r] = q < S ? g_D[q] : 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st_full[sb]);
+      return true;
+    };
+    bool sok = nq < 1 || stage_stats(0);
     for (int j = 0; j < nq; ++j) {
+      if (sok && j + 1 < nq) sok = stage_stats(j + 1);
       if (!mbar_wait(dq_full, j & 1, args.status, abort_flag)) break;
       tc_fence_after();
       uint32_t dq[2][32];
@@ -771,20 +786,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_empty);
+      // dQ_j * scale -> this query's 256-byte row of the staging tile, then one bulk
+      // reduction per row into the fp32 accumulator (performed in L2; per-thread vector
+      // atomics made the LSU queue and L2 the limit of this kernel's dQ path).
       const int q = j * kBQ + r;
-      if (q < S) {
-        float* dst = args.dq_acc + (static_cast<long long>(row0) + q) * H + h * 64;
-        const float sc = args.scale;
+      float* srow = reinterpret_cast<float*>(smem + BwdSmem::dq + r * kDqStride);
+      bulk_wait_read_all();  // the previous tile's reduction has read this row
+      const float sc = args.scale;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const int cc = 4 * u;
-          atomicAdd(reinterpret_cast<float4*>(dst + cc),
-                    make_float4(__uint_as_float(dq[cc >> 5][cc & 31]) * sc, __uint_as_float(dq[cc >> 5][(cc & 31) + 1]) * sc,
-                                __uint_as_float(dq[cc >> 5][(cc & 31) + 2]) * sc,
-                                __uint_as_float(dq[cc >> 5][(cc & 31) + 3]) * sc));
-        }
+      for (int k = 0; k < 16; ++k) {
+        reinterpret_cast<float4*>(srow)[k] =
+            make_float4(__uint_as_float(dq[(4 * k) >> 5][(4 * k) & 31]) * sc,
+                        __uint_as_float(dq[(4 * k + 1) >> 5][(4 * k + 1) & 31]) * sc,
+                        __uint_as_float(dq[(4 * k + 2) >> 5][(4 * k + 2) & 31]) * sc,
+                        __uint_as_float(dq[(4 * k + 3) >> 5][(4 * k + 3) & 31]) * sc);
+      }
+      fence_proxy_async_smem();
+      if (q < S) {
+        bulk_reduce_add_f32(args.dq_acc + (static_cast<long long>(row0) + q) * H + h * 64, srow, 256);
+        bulk_commit_group();
       }
     }
+    bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();

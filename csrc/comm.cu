@@ -73,7 +73,7 @@ __device__ bool wait_all_flags(int* own_flags, int D, int epoch, long long timeo
   return true;
 }
 
-__global__ void __launch_bounds__(512) dp_reduce_adamw_kernel(DpArgs a) {
+__global__ void __launch_bounds__(512, 2) dp_reduce_adamw_kernel(DpArgs a) {
   cg::grid_group grid = cg::this_grid();
   __shared__ float red[32];
   __shared__ float s_coef;
@@ -93,18 +93,40 @@ __global__ void __launch_bounds__(512) dp_reduce_adamw_kernel(DpArgs a) {
   grid.sync();
   if (reinterpret_cast<volatile float*>(a.sumsq_scratch)[1] < 0.f) return;
 
-  // ---- A: reduce my shard, norm partials
+  // ---- A: reduce my shard, norm partials.  kU float4 of every replica are in flight per
+  // thread before any is used: one remote load per thread at a time left the NVLink reads
+  // latency-bound (about 0.4 of the link rate).
+  constexpr int kU = 4;
   float acc = 0.f;
-  for (long long i = lo4 + tid; i < hi4; i += nthreads) {
-    float4 s = reinterpret_cast<const float4*>(a.grad[a.rank])[i];
+  for (long long i0 = lo4 + tid; i0 < hi4; i0 += kU * nthreads) {
+    float4 s[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long i = i0 + u * nthreads;
+      s[u] = i < hi4 ? reinterpret_cast<const float4*>(a.grad[a.rank])[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (int d = 0; d < a.D; ++d) {
       if (d == a.rank) continue;
-      const float4 g = reinterpret_cast<const float4*>(a.grad[d])[i];
-      s.x += g.x; s.y += g.y; s.z += g.z; s.w += g.w;
+      float4 g[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long long i = i0 + u * nthreads;
+        g[u] = i < hi4 ? __ldcs(reinterpret_cast<const float4*>(a.grad[d]) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        s[u].x += g[u].x; s[u].y += g[u].y; s[u].z += g[u].z; s[u].w += g[u].w;
+      }
     }
-    s.x *= a.inv_d; s.y *= a.inv_d; s.z *= a.inv_d; s.w *= a.inv_d;
-    reinterpret_cast<float4*>(a.grad[a.rank])[i] = s;
-    acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long i = i0 + u * nthreads;
+      if (i >= hi4) break;
+      float4 t = s[u];
+      t.x *= a.inv_d; t.y *= a.inv_d; t.z *= a.inv_d; t.w *= a.inv_d;
+      reinterpret_cast<float4*>(a.grad[a.rank])[i] = t;
+      acc += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    }
   }
   acc = warp_sum(acc);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -141,28 +163,41 @@ __global__ void __launch_bounds__(512) dp_reduce_adamw_kernel(DpArgs a) {
 
   // ---- C: AdamW on my shard, broadcast parameters to every replica
   const float decay = 1.f - a.lr * a.wd;
-  for (long long i = lo4 + tid; i < hi4; i += nthreads) {
-    const float4 gg = reinterpret_cast<const float4*>(a.grad[a.rank])[i];
-    if (a.zero_grad) reinterpret_cast<float4*>(a.grad[a.rank])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 p = reinterpret_cast<float4*>(a.param[a.rank])[i];
-    float4 m = reinterpret_cast<float4*>(a.m)[i];
-    float4 v = reinterpret_cast<float4*>(a.v)[i];
-    const float g4[4] = {gg.x * coef, gg.y * coef, gg.z * coef, gg.w * coef};
-    float* pp = &p.x;
-    float* mp = &m.x;
-    float* vp = &v.x;
+  constexpr int kUC = 2;  // g, p, m, v of kUC float4 in flight (64 registers: two blocks per SM)
+  for (long long i0 = lo4 + tid; i0 < hi4; i0 += kUC * nthreads) {
+    float4 gg[kUC], p[kUC], m[kUC], v[kUC];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      mp[j] = a.beta1 * mp[j] + (1.f - a.beta1) * g4[j];
-      vp[j] = a.beta2 * vp[j] + (1.f - a.beta2) * g4[j] * g4[j];
-      pp[j] = pp[j] * decay - a.step_size * mp[j] / (sqrtf(vp[j]) * a.inv_bc2_sqrt + a.eps);
+    for (int u = 0; u < kUC; ++u) {
+      const long long i = i0 + u * nthreads;
+      if (i < hi4) {
+        gg[u] = reinterpret_cast<const float4*>(a.grad[a.rank])[i];
+        p[u] = reinterpret_cast<const float4*>(a.param[a.rank])[i];
+        m[u] = reinterpret_cast<const float4*>(a.m)[i];
+        v[u] = reinterpret_cast<const float4*>(a.v)[i];
+      }
     }
-    reinterpret_cast<float4*>(a.m)[i] = m;
-    reinterpret_cast<float4*>(a.v)[i] = v;
-    const uint2 sh = make_uint2(pack_bf16x2(p.x, p.y), pack_bf16x2(p.z, p.w));
-    for (int d = 0; d < a.D; ++d) {
-      reinterpret_cast<float4*>(a.param[d])[i] = p;
-      if (a.shadow[d]) reinterpret_cast<uint2*>(a.shadow[d])[i] = sh;
+#pragma unroll
+    for (int u = 0; u < kUC; ++u) {
+      const long long i = i0 + u * nthreads;
+      if (i >= hi4) break;
+      if (a.zero_grad) reinterpret_cast<float4*>(a.grad[a.rank])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float g4[4] = {gg[u].x * coef, gg[u].y * coef, gg[u].z * coef, gg[u].w * coef};
+      float* pp = &p[u].x;
+      float* mp = &m[u].x;
+      float* vp = &v[u].x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mp[j] = a.beta1 * mp[j] + (1.f - a.beta1) * g4[j];
+        vp[j] = a.beta2 * vp[j] + (1.f - a.beta2) * g4[j] * g4[j];
+        pp[j] = pp[j] * decay - a.step_size * mp[j] / (sqrtf(vp[j]) * a.inv_bc2_sqrt + a.eps);
+      }
+      reinterpret_cast<float4*>(a.m)[i] = m[u];
+      reinterpret_cast<float4*>(a.v)[i] = v[u];
+      const uint2 sh = make_uint2(pack_bf16x2(p[u].x, p[u].y), pack_bf16x2(p[u].z, p[u].w));
+      for (int d = 0; d < a.D; ++d) {
+        reinterpret_cast<float4*>(a.param[d])[i] = p[u];
+        if (a.shadow[d]) reinterpret_cast<uint2*>(a.shadow[d])[i] = sh;
+      }
     }
   }
   if (a.zero_grad) {

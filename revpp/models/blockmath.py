@@ -25,6 +25,7 @@ fp32, GEMMs in bf16, F/G outputs rounded to bf16 before the fp32 residual add.
 from __future__ import annotations
 
 import math
+import os
 from types import SimpleNamespace
 from typing import List, Optional
 
@@ -140,12 +141,36 @@ class KernelMath:
         self.heads = heads
         self._views: dict = {}
         self._scratch: dict = {}
+        self._side: dict = {}
+        # weight-gradient GEMMs on a side stream, concurrent with the input-gradient chain
+        # (each pair reads the same operands; the persistent GEMM that starts second fills
+        # the SMs that the first one's last wave leaves idle)
+        self.wgrad_overlap = os.environ.get("REVPP_WGRAD_OVERLAP", "1") != "0"
 
     def views(self, blk: EncoderBlock) -> _WeightViews:
         v = self._views.get(id(blk))
         if v is None:
             v = self._views[id(blk)] = _WeightViews(self.flat, blk)
         return v
+
+    def side_stream(self) -> Optional[torch.cuda.Stream]:
+        """The weight-gradient stream paired with the current stream (None: no overlap)."""
+        if not self.wgrad_overlap:
+            return None
+        cur = torch.cuda.current_stream()
+        st = self._side.get(cur.cuda_stream)
+        if st is None:
+            st = self._side[cur.cuda_stream] = torch.cuda.Stream(device=self.flat.device)
+        return st
+
+    def _wgrad(self, side, dy, x, dw) -> None:
+        """dw += dy^T x, on ``side`` after everything queued so far on the current stream."""
+        if side is None:
+            self.ops.linear_wgrad(dy, x, dw)
+            return
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.ops.linear_wgrad(dy, x, dw)
 
     def scratch(self, name: str, shape, dtype) -> torch.Tensor:
         """Reusable per-stream buffer (same stream -> same buffer)."""
@@ -235,10 +260,11 @@ class KernelMath:
         if dy_bf16 is None:
             dy_bf16 = self.scratch("g_dyb", (M, H), torch.bfloat16)
             ops.cast_colsum(dy2d, out=dy_bf16, colsum=w.d_b2)           # bf16(dy), db2 += sum(dy)
-        ops.linear_wgrad(dy_bf16, ctx.h, w.d_w2)                        # dW2 += dy^T h
+        side = self.side_stream()
+        self._wgrad(side, dy_bf16, ctx.h, w.d_w2)                      # dW2 += dy^T h
         # du = (dy W2) * gelu'(u), db1 += sum(du) in the same epilogue
         ops.linear_dgrad(dy_bf16, w.w2, du, epi=ops.EPI_DGELU, aux=ctx.u, colsum=w.d_b1)
-        ops.linear_wgrad(du, ctx.b, w.d_w1)                             # dW1 += du^T LN2(x)
+        self._wgrad(side, du, ctx.b, w.d_w1)                           # dW1 += du^T LN2(x)
         ops.linear_dgrad(du, w.w1, dln)                                 # d LN2 out = du W1
         if out is None:
             out = torch.empty_like(dy)
@@ -246,6 +272,8 @@ class KernelMath:
         ops.layernorm_bwd(dln, ctx.x.view(M, H), w.ln2_w, ctx.mean, ctx.rstd, dgamma=w.d_ln2_w, dbeta=w.d_ln2_b,
                           resid=None if resid_grad is None else resid_grad.view(M, H), dx_f32=out.view(M, H),
                           dx_bf16=dxb, colsum=out_colsum)
+        if side is not None:  # scratch and saved activations are reused after this VJP
+            torch.cuda.current_stream().wait_stream(side)
         ctx.dx_bf16 = dxb
         ctx.dx_colsum_done = out_colsum is not None
         return out
@@ -272,17 +300,20 @@ class KernelMath:
         dq_acc = self.scratch("f_dqacc", (M, H), torch.float32)
         dbuf = self.scratch("f_D", (B, self.heads, S), torch.float32)
         dln = self.scratch("f_dln", (M, H), torch.bfloat16)
-        ops.linear_wgrad(dy_bf16, ctx.o, w.d_wo)                        # dWo += dy^T o
+        side = self.side_stream()
+        self._wgrad(side, dy_bf16, ctx.o, w.d_wo)                      # dWo += dy^T o
         ops.linear_dgrad(dy_bf16, w.wo, do)                             # do = dy Wo
         # dqkv, and dbqkv += sum(dqkv) fused into the attention backward's write-out
         ops.attention_bwd(ctx.qkv, ctx.o, do, ctx.lse, dqkv, dq_acc, dbuf, B, S, self.heads, colsum=w.d_bqkv)
-        ops.linear_wgrad(dqkv, ctx.a, w.d_wqkv)                         # dWqkv += dqkv^T LN1(x)
+        self._wgrad(side, dqkv, ctx.a, w.d_wqkv)                       # dWqkv += dqkv^T LN1(x)
         ops.linear_dgrad(dqkv, w.wqkv, dln)                             # d LN1 out = dqkv Wqkv
         if out is None:
             out = torch.empty_like(dy)
         ops.layernorm_bwd(dln, ctx.x.view(M, H), w.ln1_w, ctx.mean, ctx.rstd, dgamma=w.d_ln1_w, dbeta=w.d_ln1_b,
                           resid=None if resid_grad is None else resid_grad.view(M, H), dx_f32=out.view(M, H),
                           dx_bf16=out_bf16, colsum=out_colsum)
+        if side is not None:
+            torch.cuda.current_stream().wait_stream(side)
         return out
 
 
