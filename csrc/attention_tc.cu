@@ -374,10 +374,11 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 //   dK  += dS^T Q_j     (same)                               -> TMEM cols [320, 384)
 //   dQ_j = dS K         (M 128 queries, N 64, K 128 keys; dS read MN-major from the dS^T
 //                        tile)                               -> TMEM cols [384, 448)
-//   dQ warps (one thread per query) add dQ_j * scale into an fp32 buffer with atomics.
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK dV, 6-9 dQ
+//   dQ warps (one thread per query) stage dQ_j * scale in shared memory and add each
+//       256-byte row to an fp32 buffer with a bulk reduction (performed in L2).
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK, 6-9 dQ
 // and the LSE / D rows of the next query tile (double-buffered in smem, so the softmax
-// warps never wait for one another), 10-13 softmax (queries 64-127).
+// warps never wait for one another), 10-13 softmax (queries 64-127) / final dV.
 // Overlap: as soon as the softmax of tile j has consumed S^T / dP^T, the issuer starts
 // S^T / dP^T of tile j+1 and only then the dV / dK / dQ MMAs of tile j, so the softmax of
 // tile j+1 runs while the tensor core works on tile j.  dS^T is therefore double-buffered
@@ -456,7 +457,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* grp_bar = bar + 13;   // the eight softmax warps' own barrier (bounded waits)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* cs_bar = bar + 16;    // the four dK / dV warps' column sums are in shared memory
+  uint64_t* cs_bar = bar + 16;    // the eight dK / dV warps' column sums are in shared memory
   uint64_t* pt_free = bar + 17;   // the dV MMAs of a tile have read P^T from TMEM
   uint64_t* st_full = bar + 18;   // [2] LSE / D rows of a query tile staged
   uint64_t* st_empty = bar + 20;  // [2] the eight softmax warps are done with them
@@ -487,7 +488,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(kv_done, 1);
     mbar_init(drain, 1);
     mbar_init(grp_bar, 8);
-    mbar_init(cs_bar, 4);
+    mbar_init(cs_bar, 8);
     mbar_init(pt_free, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 4);
@@ -653,44 +654,57 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // this group's 64 queries are 64-query swizzle chunk `grp` of the dS^T tile
       uint8_t* drow = ds_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
       const float sl2 = args.scale_log2;
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * grp + cc;  // 32-query chunk of the tile
-        uint32_t sv[32], dp[32];
-        tmem_ld32(tmem + lane_off + c * 32, sv);
-        tmem_ld32(tmem + lane_off + 128 + c * 32, dp);
-        tmem_wait_ld();
-        uint32_t pw[16], dw[16];
+      // Four 16-query sub-chunks, software-pipelined: the S^T / dP^T columns of sub-chunk
+      // k + 1 are loaded from TMEM while sub-chunk k is computed.
+      uint32_t sv[2][16], dp[2][16];
+      tmem_ld16(tmem + lane_off + grp * 64, sv[0]);
+      tmem_ld16(tmem + lane_off + 128 + grp * 64, dp[0]);
+      tmem_wait_ld();
+      tmem_regs_ready(sv[0]);
+      tmem_regs_ready(dp[0]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int cur = k & 1;
+        if (k < 3) {
+          tmem_ld16(tmem + lane_off + grp * 64 + 16 * (k + 1), sv[cur ^ 1]);
+          tmem_ld16(tmem + lane_off + 128 + grp * 64 + 16 * (k + 1), dp[cur ^ 1]);
+        }
+        const int q4 = (grp * 64 + 16 * k) / 4;  // first float4 of this sub-chunk's LSE / D
+        uint32_t pw[8], dw[8];
         if (key_ok) {
 #pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 L = s_lse4[c * 8 + e4];
-            const float4 Dq = s_D4[c * 8 + e4];
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 0]), sl2, -L.x));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 1]), sl2, -L.y));
-            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 2]), sl2, -L.z));
-            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 3]), sl2, -L.w));
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 L = s_lse4[q4 + e4];
+            const float4 Dq = s_D4[q4 + e4];
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 0]), sl2, -L.x));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 1]), sl2, -L.y));
+            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 2]), sl2, -L.z));
+            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 3]), sl2, -L.w));
             const uint32_t pp0 = pack_bf16x2(p0, p1), pp1 = pack_bf16x2(p2, p3);
             const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
             pw[2 * e4] = pp0;
             pw[2 * e4 + 1] = pp1;
-            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[4 * e4 + 0]) - Dq.x),
-                                     r0.y * (__uint_as_float(dp[4 * e4 + 1]) - Dq.y));
-            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[4 * e4 + 2]) - Dq.z),
-                                         r1.y * (__uint_as_float(dp[4 * e4 + 3]) - Dq.w));
+            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[cur][4 * e4 + 0]) - Dq.x),
+                                     r0.y * (__uint_as_float(dp[cur][4 * e4 + 1]) - Dq.y));
+            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[cur][4 * e4 + 2]) - Dq.z),
+                                         r1.y * (__uint_as_float(dp[cur][4 * e4 + 3]) - Dq.w));
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) pw[e] = dw[e] = 0u;
+          for (int e = 0; e < 8; ++e) pw[e] = dw[e] = 0u;
         }
-        // P^T: queries 32c .. 32c + 31 are TMEM columns kTmemPt + 16c .. + 15 of this key's lane
-        tmem_st16(tmem + lane_off + kTmemPt + 16 * c, pw);
-        // dS^T: 32 queries = 64 bytes = four 16-byte units of the row
+        // P^T: the 16 queries are TMEM columns kTmemPt + 32 grp + 8k .. + 7 of this key's lane
+        tmem_st8(tmem + lane_off + kTmemPt + 32 * grp + 8 * k, pw);
+        // dS^T: 16 queries = 32 bytes = 16-byte units 2k, 2k + 1 of this group's row
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int u = cc * 4 + t;
-          const uint32_t off = (u ^ sw) << 4;
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t off = ((2 * k + t) ^ sw) << 4;
           *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
+        }
+        if (k < 3) {
+          tmem_wait_ld();
+          tmem_regs_ready(sv[cur ^ 1]);
+          tmem_regs_ready(dp[cur ^ 1]);
         }
       }
       __syncwarp();
@@ -701,17 +715,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // final dK, dV for this warp's keys (group 0); the decision is made warp-uniform since
-    // the column sums below shuffle across all lanes
-    bool fin = grp == 0 && ok;
+    // final dK (group 0) and dV (group 1) for this warp's keys; the decision is made
+    // warp-uniform since the column sums below shuffle across all lanes
+    bool fin = ok;
     if (fin) fin = mbar_wait(kv_done, 0, args.status, abort_flag);
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       const long long ld = 3LL * H;
       const long long base = (static_cast<long long>(row0) + k0 + r) * ld + h * 64;
-      // dK (TMEM cols 320..383, scaled) then dV (256..319), 32 columns per load
+      // dK (TMEM cols 320..383, scaled) or dV (256..319), 32 columns per load
 #pragma unroll 1
-      for (int part = 0; part < 4; ++part) {
+      for (int part = 2 * grp; part < 2 * grp + 2; ++part) {
         const bool is_k = part < 2;
         const int half = part & 1;
         uint32_t v[32];
@@ -742,11 +756,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       if (args.colsum != nullptr) {
-        // One atomic per column and CTA: the 4 warps' sums are added here first (an atomic
-        // per warp put 4 x (B * S / 128) same-address atomics in L2's queue per column).
+        // One atomic per column and CTA: the 4 key quarters' sums are added here first (an
+        // atomic per warp put 4 x (B * S / 128) same-address atomics in L2's queue per column).
         __syncwarp();
         if (lane == 0) mbar_arrive(cs_bar);
-        if (quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
+        if (grp == 0 && quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
           const float* red = reinterpret_cast<const float*>(smem + BwdSmem::dst);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {

@@ -214,6 +214,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 
+// Store of 8 consecutive 32-bit columns of this warp's 32 TMEM lanes (one row per thread).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :
+               : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+// Ties registers filled by an earlier tcgen05.ld to the point after tcgen05.wait::ld, so the
+// compiler cannot move their uses above the wait when loads are software-pipelined.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // ---------------------------------------------------------------- clusters / 2-SM MMA
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
