@@ -2,24 +2,27 @@
 // Head dim 64; same interface and numerics as attn_fwd in attention.cu (qkv packed as
 // nn.MultiheadAttention's in_proj output, o [B*S, H] bf16, lse [B, heads, S] fp32).
 //
-// One CTA per (query tile of 128 rows, head, sequence); 64-key tiles.
+// One CTA per (query tile of 128 rows, head, sequence); 64-key tiles.  Two softmax
+// warpgroups split the key tiles of the CTA: group w takes tiles j with j % 2 == w, with
+// its own TMEM scores S[w], output accumulator O[w], P tile, running maximum and sum, so
+// the groups never wait for each other until the end, where group 0 merges the two
+// partial results (O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / l).  Sixteen softmax warps
+// per SM (two CTAs) keep the exp / max / pack work of one group running while the other
+// waits on the tensor core.
 //   warp 0     : TMA producer - Q once, then K_j / V_j into a 3-deep ring (no multicast)
 //   warp 1     : TMEM allocator and MMA issuer (one thread):
-//                  S_j  = Q K_j^T   (M 128, N 64, K 64)  -> TMEM S[j % 2]
-//                  O   += P_j V_j   (M 128, N 64, K 64)  -> TMEM O (accumulated over j)
-//                S_{j+1} is issued before waiting for P_j, so the tensor core works on the
-//                next scores while the softmax warps handle the current ones.
-//   warps 2-5  : softmax, one thread per query row: S row from TMEM, P_j = exp2(S * scale
-//                - m) as bf16 into a 128-byte-swizzled smem tile (the MMA's A operand),
-//                running row sum l in fp32.
-// The output accumulates in TMEM with a reference maximum m that is raised only when a
-// row's new maximum exceeds it by more than 8 (log2 units): P then stays <= 256, and the
-// rescale (O *= 2^(m_old - m_new) through tcgen05.ld / st, after the previous P V has
-// landed) is rare, so the per-tile work of a softmax thread is one TMEM load, the max,
-// the exponentials and the P store - no per-tile output correction.  Softmax is
-// invariant to the reference maximum, so the result equals the exact-max formulation up
-// to rounding.
-// Shared memory ~97 KB and 256 TMEM columns, so two CTAs share an SM.
+//                  S_j    = Q K_j^T   (M 128, N 64, K 64)  -> TMEM S[j % 2]
+//                  O[j%2] += P_j V_j  (M 128, N 64, K 64)
+//                S_{j+1} is issued before waiting for P_j.
+//   warps 2-5  : softmax group 0 (even key tiles); warps 6-9: group 1 (odd key tiles);
+//                one thread per query row: S row from TMEM, P_j = exp2(S * scale - m) as
+//                bf16 into a 128-byte-swizzled smem tile (the MMA's A operand).
+// Each group keeps a reference maximum m that is raised only when a tile's maximum
+// exceeds it by more than 8 (log2 units): P stays <= 256, and the rescale of O (through
+// tcgen05.ld / st, after the group's previous P V has landed) is rare.  Softmax is
+// invariant to the reference maximum, so this equals the exact-max formulation up to
+// rounding.
+// Shared memory ~98 KB and 256 TMEM columns, so two CTAs share an SM.
 #include "common.cuh"
 #include "host.h"
 
@@ -30,11 +33,11 @@ constexpr int kQ = 128;      // query rows per CTA
 constexpr int kKV = 64;      // keys per tile
 constexpr int kDh = 64;      // head dim
 constexpr int kStages = 3;   // K/V ring depth
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kQBytes = kQ * kDh * 2;     // 16 KB
 constexpr uint32_t kKVBytes = kKV * kDh * 2;   // 8 KB (one of K or V)
 constexpr uint32_t kPBytes = kQ * kKV * 2;     // 16 KB
-constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + O (64)
+constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + O[2] (64 each)
 constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8
 constexpr uint32_t kIdescS = idesc_bf16(kQ, kKV, false, false);
@@ -45,8 +48,9 @@ struct SmemLayout {
   static constexpr uint32_t q = 0;
   static constexpr uint32_t k = q + kQBytes;                      // kStages x 8 KB
   static constexpr uint32_t v = k + kStages * kKVBytes;           // kStages x 8 KB
-  static constexpr uint32_t p = v + kStages * kKVBytes;           // 2 x 16 KB
-  static constexpr uint32_t bars = p + 2 * kPBytes;
+  static constexpr uint32_t p = v + kStages * kKVBytes;           // 2 x 16 KB (one per group)
+  static constexpr uint32_t stats = p + 2 * kPBytes;              // group 1's m, l per row
+  static constexpr uint32_t bars = stats + 2 * kQ * 4;
   static constexpr uint32_t total = bars + 256;
 };
 }  // namespace
@@ -57,7 +61,16 @@ struct AttnTcArgs {
   int S, heads;
   float scale_log2;
   int* status;
+  // optional [grid][8] globaltimer stamps of the CTA's phases (measurement aid)
+  unsigned long long* phase_ns = nullptr;
 };
+
+__device__ __forceinline__ void phase_stamp(unsigned long long* ph, int k) {
+  if (ph != nullptr) {
+    const long long cta = blockIdx.x + static_cast<long long>(gridDim.x) * (blockIdx.y + static_cast<long long>(gridDim.y) * blockIdx.z);
+    ph[cta * 8 + k] = globaltimer_ns();
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
@@ -67,16 +80,21 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;              // [kStages]
-  uint64_t* kv_empty = kv_full + kStages;   // [kStages]
-  uint64_t* s_full = kv_empty + kStages;    // [2]
+  uint64_t* k_full = bar + 1;               // [kStages]
+  uint64_t* k_empty = k_full + kStages;     // [kStages] freed by S_j
+  uint64_t* v_full = k_empty + kStages;     // [kStages]
+  uint64_t* v_empty = v_full + kStages;     // [kStages] freed by P_j V_j
+  uint64_t* s_full = v_empty + kStages;     // [2] per group
   uint64_t* s_empty = s_full + 2;           // [2]
   uint64_t* p_full = s_empty + 2;           // [2]
   uint64_t* p_empty = p_full + 2;           // [2]
-  uint64_t* pv_done = p_empty + 2;          // completes once per P V (in order)
-  uint64_t* drain = pv_done + 1;
+  uint64_t* pv_done = p_empty + 2;          // [2] once per P V of the group (in order)
+  uint64_t* comb = pv_done + 2;             // group 1's m, l are in shared memory
+  uint64_t* drain = comb + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_m1 = reinterpret_cast<float*>(smem + SmemLayout::stats);
+  float* s_l1 = s_m1 + kQ;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -89,16 +107,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(pv_done, 1);
+    mbar_init(comb, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -115,32 +136,47 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) phase_stamp(args.phase_ns, 0);
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
       mbar_arrive_expect_tx(q_full, kQBytes);
       tma_load_2d(smem + SmemLayout::q, &tmQ, q_full, h * kDh, row0 + q0);
-      uint32_t issued = 0, issued_par = 0;
-      for (int j = 0; j < nkv; ++j) {
+      // K_j as soon as S_{j-3} has read its stage, V_j once P_{j-3} V_{j-3} has: keys run
+      // ahead of values, so the scores of a group's next tile never wait for P V
+      uint32_t issued = 0, issued_par = 0;  // bits 0..2: K stages, 3..5: V stages
+      int jk = 0, jv = 0;
+      while (jv < nkv) {
+        const bool take_k = jk < nkv && jk < jv + kStages;
+        const int j = take_k ? jk : jv;
         const int st = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, args.status, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
-        tma_load_2d(smem + SmemLayout::k + st * kKVBytes, &tmKV, &kv_full[st], H + h * kDh, row0 + j * kKV);
-        tma_load_2d(smem + SmemLayout::v + st * kKVBytes, &tmKV, &kv_full[st], 2 * H + h * kDh, row0 + j * kKV);
-        issued |= 1u << st;
-        issued_par = (issued_par & ~(1u << st)) | (ph << st);
+        uint64_t* empty = take_k ? &k_empty[st] : &v_empty[st];
+        uint64_t* full = take_k ? &k_full[st] : &v_full[st];
+        if (!mbar_wait(empty, ph ^ 1u, args.status, abort_flag)) break;
+        mbar_arrive_expect_tx(full, kKVBytes);
+        tma_load_2d(smem + (take_k ? SmemLayout::k : SmemLayout::v) + st * kKVBytes, &tmKV, full,
+                    (take_k ? H : 2 * H) + h * kDh, row0 + j * kKV);
+        const int bit = st + (take_k ? 0 : kStages);
+        issued |= 1u << bit;
+        issued_par = (issued_par & ~(1u << bit)) | (ph << bit);
+        if (take_k) {
+          ++jk;
+        } else {
+          ++jv;
+        }
       }
       if (*abort_flag) {
         // let in-flight copies land before the CTA exits
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
-        for (int s = 0; s < kStages; ++s) {
-          if (!(issued & (1u << s))) continue;
+        for (int bit = 0; bit < 2 * kStages; ++bit) {
+          if (!(issued & (1u << bit))) continue;
+          uint64_t* full = bit < kStages ? &k_full[bit] : &v_full[bit - kStages];
           const uint64_t t1 = globaltimer_ns();
-          while (!mbar_try_wait(&kv_full[s], (issued_par >> s) & 1u) && globaltimer_ns() - t1 < 100000000ull) {
+          while (!mbar_try_wait(full, (issued_par >> bit) & 1u) && globaltimer_ns() - t1 < 100000000ull) {
           }
         }
       }
@@ -153,173 +189,210 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t v_addr = smem_u32(smem + SmemLayout::v);
       const uint32_t p_addr = smem_u32(smem + SmemLayout::p);
       bool ok = mbar_wait(q_full, 0, args.status, abort_flag);
-      auto issue_pv = [&](int j) -> bool {
-        const int pb = j & 1;
-        const uint32_t par = (j >> 1) & 1;
-        // P_j is in smem, and any rescale of O by the softmax threads has been stored
-        if (!mbar_wait(&p_full[pb], par, args.status, abort_flag)) return false;
-        tc_fence_after();
+      // S_j = Q K_j^T into S[j % 2], once group j % 2 has read S_{j-2}
+      auto issue_s = [&](int j) -> bool {
         const int st = j % kStages;
-#pragma unroll
-        for (int k = 0; k < kKV / 16; ++k) {
-          const uint64_t ad = sdesc_sw128(p_addr + pb * kPBytes + k * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_addr + st * kKVBytes + k * 2048, 8192, 1024);
-          umma_bf16_ss(tmem + kTmemO, ad, bd, kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&p_empty[pb]);
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int sb = j & 1;
-        if (!mbar_wait(&kv_full[st], ph, args.status, abort_flag)) break;
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) break;
+        const int w = j & 1;
+        if (!mbar_wait(&k_full[st], (j / kStages) & 1, args.status, abort_flag)) return false;
+        if (j == 0) phase_stamp(args.phase_ns, 1);  // Q and the first K have landed
+        if (!mbar_wait(&s_empty[w], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + sb * kKV;
 #pragma unroll
         for (int k = 0; k < kDh / 16; ++k) {
           const uint64_t ad = sdesc_sw128(q_addr + k * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(k_addr + st * kKVBytes + k * 32, 16, 1024);
-          umma_bf16_ss(d, ad, bd, kIdescS, k > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + w * kKV, ad, bd, kIdescS, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) {
+        umma_commit(&s_full[w]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      // O[j % 2] += P_j V_j, once group j % 2 has stored P_j (and any rescale of O)
+      auto issue_pv = [&](int j) -> bool {
+        const int w = j & 1;
+        const int st = j % kStages;
+        if (!mbar_wait(&p_full[w], (j >> 1) & 1, args.status, abort_flag)) return false;
+        if (!mbar_wait(&v_full[st], (j / kStages) & 1, args.status, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kKV / 16; ++k) {
+          const uint64_t ad = sdesc_sw128(p_addr + w * kPBytes + k * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(v_addr + st * kKVBytes + k * 2048, 8192, 1024);
+          umma_bf16_ss(tmem + kTmemO + w * kDh, ad, bd, kIdescPV, (j >= 2 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[w]);
+        umma_commit(&p_empty[w]);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      // scores run two tiles ahead of P V: S_{j+2} (the same group's next tile) is issued
+      // as soon as that group has read S_j, before waiting for its P_j
+      for (int j = 0; ok && j < 2 && j < nkv; ++j) ok = issue_s(j);
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (j + 2 < nkv && !issue_s(j + 2)) {
+          ok = false;
+          break;
+        }
+        if (!issue_pv(j)) {
           ok = false;
           break;
         }
       }
-      if (ok && nkv >= 1) issue_pv(nkv - 1);
       umma_commit(drain);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
       }
     }
   } else {
-    // ------------------------------------------------------------------ softmax
+    // ------------------------------------------------------------------ softmax groups
+    const int w = (warp - 2) >> 2;               // group: key tiles j with j % 2 == w
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;           // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* p_base = smem + SmemLayout::p;
+    const uint32_t o_col = kTmemO + w * kDh;
+    uint8_t* prow = smem + SmemLayout::p + w * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
     float m = -INFINITY, l = 0.f;
     const float sl2 = args.scale_log2;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      const uint32_t par = (j >> 1) & 1;
-      if (!mbar_wait(&s_full[sb], par, args.status, abort_flag)) {
+    int t = 0;  // this group's tile count
+    for (int j = w; j < nkv; j += 2, ++t) {
+      const uint32_t par = t & 1;
+      if (!mbar_wait(&s_full[w], par, args.status, abort_flag)) {
         ok = false;
         break;
       }
+      if (t == 0 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 2);  // first scores ready
       tc_fence_after();
       uint32_t sr[2][32];
-      tmem_ld32(tmem + lane_off + sb * kKV, sr[0]);
-      tmem_ld32(tmem + lane_off + sb * kKV + 32, sr[1]);
+      tmem_ld32(tmem + lane_off + w * kKV, sr[0]);
+      tmem_ld32(tmem + lane_off + w * kKV + 32, sr[1]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);
-      // raw scores; the softmax scale (> 0) is applied after the max, folded into one FMA
-      float sv[kKV];
-#pragma unroll
-      for (int c = 0; c < kKV; ++c) sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      if (lane == 0) mbar_arrive(&s_empty[w]);
+      // raw scores (the softmax scale, > 0, is applied after the max, folded into one FMA);
+      // keys past the sequence end read as -inf
       const int kbase = j * kKV;
       if (kbase + kKV > S) {
 #pragma unroll
         for (int c = 0; c < kKV; ++c)
-          if (kbase + c >= S) sv[c] = -INFINITY;
+          if (kbase + c >= S) sr[c >> 5][c & 31] = 0xff800000u;
       }
+#define SV(c) __uint_as_float(sr[(c) >> 5][(c) & 31])
       // row max as 8 independent chains
       float pm[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = sv[i];
+      for (int i = 0; i < 8; ++i) pm[i] = SV(i);
 #pragma unroll
-      for (int c = 8; c < kKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], sv[c]);
+      for (int c = 8; c < kKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], SV(c));
       const float tmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
-      if (j == 0) {
-        m = tmx;  // key 0 is always valid, so m is finite
+      if (t == 0) {
+        m = tmx;  // key 0 of every tile is below S, so m is finite
       } else if (__any_sync(0xffffffffu, tmx > m + kRescaleThreshold)) {
-        // raise the reference maximum of this warp's rows; O holds P_0..P_{j-1} V once
-        // the previous P V has completed
+        // raise the reference maximum of this warp's rows; O[w] holds this group's earlier
+        // tiles once its previous P V has completed
         const float mn = fmaxf(m, tmx);
         const float alpha = ex2_approx(m - mn);
         m = mn;
         l *= alpha;
-        if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, args.status, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[w], (t - 1) & 1, args.status, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_off + kTmemO + 32 * hh, o);
+#pragma unroll 1
+        for (int hh = 0; hh < 4; ++hh) {
+          uint32_t o[16];
+          tmem_ld16(tmem + lane_off + o_col + 16 * hh, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem + lane_off + kTmemO + 32 * hh, o);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(tmem + lane_off + o_col + 16 * hh, o);
         }
         tmem_wait_st();
       }
       // P_j -> smem (A operand of P V, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7))
-      if (!mbar_wait(&p_empty[sb], par ^ 1u, args.status, abort_flag)) {
+      if (!mbar_wait(&p_empty[w], par ^ 1u, args.status, abort_flag)) {
         ok = false;
         break;
       }
-      uint8_t* prow = p_base + sb * kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
       float rsp[8];  // row-sum partials, one per 16-byte unit
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
+        uint32_t wd[4];
         float ps = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(sv[8 * c + 2 * e], sl2, -m));
-          const float p1 = ex2_approx(fmaf(sv[8 * c + 2 * e + 1], sl2, -m));
+          const float p0 = ex2_approx(fmaf(SV(8 * c + 2 * e), sl2, -m));
+          const float p1 = ex2_approx(fmaf(SV(8 * c + 2 * e + 1), sl2, -m));
           ps += p0 + p1;
-          w[e] = pack_bf16x2(p0, p1);
+          wd[e] = pack_bf16x2(p0, p1);
         }
         rsp[c] = ps;
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
       }
+#undef SV
       l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (lane == 0) mbar_arrive(&p_full[w]);
     }
-    // the last P V completes the output
-    bool fin = ok && nkv >= 1;
-    if (fin) fin = mbar_wait(pv_done, (nkv - 1) & 1, args.status, abort_flag);
-    if (__all_sync(0xffffffffu, fin)) {
-      tc_fence_after();
-      const int q = q0 + r;
-      const float inv = 1.f / l;
-      uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh);
+    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 3);  // group 0's last P handed over
+    // this group's last P V has landed in O[w]
+    bool fin = ok;
+    if (fin && t > 0) fin = mbar_wait(&pv_done[w], (t - 1) & 1, args.status, abort_flag);
+    if (w == 1) {
+      // group 1 hands its maximum and sum to group 0 (m = -inf, l = 0 without key tiles)
+      s_m1[r] = fin ? m : -INFINITY;
+      s_l1[r] = fin ? l : 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(comb);
+    } else {
+      fin = fin && mbar_wait(comb, 0, args.status, abort_flag);
+      if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // merge starts
+      if (__all_sync(0xffffffffu, fin)) {
+        tc_fence_after();
+        const float m1 = s_m1[r], l1 = s_l1[r];
+        const float mx = fmaxf(m, m1);
+        const float a0 = ex2_approx(m - mx);
+        const float a1 = l1 > 0.f ? ex2_approx(m1 - mx) : 0.f;
+        const float lt = l * a0 + l1 * a1;
+        const float inv = 1.f / lt;
+        const float c0 = a0 * inv, c1 = a1 * inv;
+        const bool two = nkv >= 2;  // group 1 has key tiles (uniform over the CTA)
+        const int q = q0 + r;
+        uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh);
+#pragma unroll 1
+        for (int hh = 0; hh < 4; ++hh) {
+          uint32_t o0[16], o1[16];
+          tmem_ld16(tmem + lane_off + kTmemO + 16 * hh, o0);
+          if (two) tmem_ld16(tmem + lane_off + kTmemO + kDh + 16 * hh, o1);
+          tmem_wait_ld();
+          if (q < S) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_off + kTmemO + 32 * hh, o);
-        tmem_wait_ld();
-        if (q < S) {
+            for (int c = 0; c < 2; ++c) {
+              float f[8];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * c + e]) * inv;
-            dst[4 * hh + c] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                                         pack_bf16x2(f[6], f[7]));
+              for (int e = 0; e < 8; ++e) {
+                const float x1 = two ? __uint_as_float(o1[8 * c + e]) * c1 : 0.f;
+                f[e] = fmaf(__uint_as_float(o0[8 * c + e]), c0, x1);
+              }
+              dst[2 * hh + c] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                           pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            }
           }
         }
+        if (q < S)
+          args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (mx + log2f(lt)) * 0.69314718055994531f;
+        if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 5);  // merge and stores issued
       }
-      if (q < S) args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (m + log2f(l)) * 0.69314718055994531f;
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) phase_stamp(args.phase_ns, 6);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -327,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
-                 int64_t heads) {
+                 int64_t heads, const c10::optional<torch::Tensor>& phase_ns) {
   check_cuda_bf16(qkv, "qkv");
   check_cuda_bf16(out, "out");
   check_cuda_f32(lse, "lse");
@@ -347,6 +420,12 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
   a.heads = static_cast<int>(heads);
   a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kDh)));
   a.status = status_device_ptr();
+  if (phase_ns.has_value() && phase_ns->defined()) {
+    REVPP_CHECK(phase_ns->scalar_type() == at::kLong && phase_ns->is_cuda() && phase_ns->is_contiguous() &&
+                    phase_ns->numel() >= ((S + kQ - 1) / kQ) * heads * B * 8,
+                "phase_ns must be a CUDA int64 tensor of grid x 8 entries");
+    a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
+  }
   constexpr int smem = SmemLayout::total + 1024;
   static int configured_for = -1;
   int dev = 0;
@@ -419,6 +498,7 @@ struct AttnBwdTcArgs {
   float scale, scale_log2;
   int* status;
   float* colsum = nullptr;  // [3H] fp32 or null: += column sums of the bf16 dK / dV written here
+  unsigned long long* phase_ns = nullptr;  // optional [grid][8] globaltimer stamps (measurement aid)
 };
 
 // Column sums over the 32 rows (lanes) of a warp: v holds this lane's 32 columns; returns
@@ -461,6 +541,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* pt_free = bar + 17;   // the dV MMAs of a tile have read P^T from TMEM
   uint64_t* st_full = bar + 18;   // [2] LSE / D rows of a query tile staged
   uint64_t* st_empty = bar + 20;  // [2] the eight softmax warps are done with them
+  uint64_t* s_free = bar + 22;    // the eight softmax warps have read S^T / dP^T of a tile
   float* s_stats = reinterpret_cast<float*>(smem + BwdSmem::stats);  // [2][256]: lse*log2e, D
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -490,6 +571,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(grp_bar, 8);
     mbar_init(cs_bar, 8);
     mbar_init(pt_free, 1);
+    mbar_init(s_free, 8);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&st_full[i], 4);
       mbar_init(&st_empty[i], 8);
@@ -509,6 +591,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) phase_stamp(args.phase_ns, 0);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -563,6 +646,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(s_full);
       };
       bool ok = mbar_wait(kv_full, 0, args.status, abort_flag) && mbar_wait(&q_full[0], 0, args.status, abort_flag);
+      phase_stamp(args.phase_ns, 1);  // K, V and the first Q / dO have landed
       if (ok) {
         tc_fence_after();
         issue_s(0);
@@ -571,15 +655,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int bb = j & 1;
         const uint32_t jp = j & 1;
         const uint32_t pb = j & 1;
-        // softmax of tile j is done: S/dP TMEM is free, P^T / dS^T of tile j are in buffer pb
-        if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
+        // the softmax warps have read S^T / dP^T of tile j from TMEM: start tile j+1 now,
+        // so its scores are computed while they finish tile j and its softmax overlaps
+        // this tile's gradient MMAs
+        if (!mbar_wait(s_free, jp, args.status, abort_flag)) break;
         tc_fence_after();
         if (j + 1 < nq) {
-          // start tile j+1 now so its softmax overlaps this tile's gradient MMAs
           if (!mbar_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status, abort_flag)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
+        // softmax of tile j is done: P^T of tile j is in TMEM, dS^T in buffer pb
+        if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
+        tc_fence_after();
         if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
         tc_fence_after();
         const uint32_t a_dsj = a_ds + pb * kSqTile;
@@ -639,6 +727,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
+      if (j == 0 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 2);  // first S^T / dP^T ready
       if (!mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) {
         ok = false;
         break;
@@ -705,6 +794,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tmem_wait_ld();
           tmem_regs_ready(sv[cur ^ 1]);
           tmem_regs_ready(dp[cur ^ 1]);
+          if (k == 2) {  // every S^T / dP^T column of this tile is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+          }
         }
       }
       __syncwarp();
@@ -717,8 +811,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     // final dK (group 0) and dV (group 1) for this warp's keys; the decision is made
     // warp-uniform since the column sums below shuffle across all lanes
+    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 3);  // last tile's P^T / dS^T handed over
     bool fin = ok;
     if (fin) fin = mbar_wait(kv_done, 0, args.status, abort_flag);
+    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // dK / dV complete in TMEM
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       const long long ld = 3LL * H;
@@ -770,6 +866,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       }
+      if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 5);  // dK written, column sums added
     }
   } else {
     // ------------------------------------------------------------------ dQ (queries)
@@ -821,10 +918,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bulk_commit_group();
       }
     }
-    bulk_wait_all();
+    // the staging tile must outlive the reductions' reads; their writes to global memory
+    // complete with the grid
+    bulk_wait_read_all();
+    if (warp == 6 && lane == 0) phase_stamp(args.phase_ns, 6);  // last dQ reduction read
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) phase_stamp(args.phase_ns, 7);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -889,7 +990,8 @@ __global__ void __launch_bounds__(256) attn_dq_convert_colsum_kernel(const float
 // gradient, fused into the dK/dV write-out and the dQ conversion.
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
-                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum) {
+                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum,
+                 const c10::optional<torch::Tensor>& phase_ns) {
   check_cuda_bf16(qkv, "qkv");
   check_cuda_bf16(out, "out");
   check_cuda_bf16(dout, "dout");
@@ -929,6 +1031,12 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
     cs = colsum->data_ptr<float>();
   }
   a.colsum = cs;
+  if (phase_ns.has_value() && phase_ns->defined()) {
+    REVPP_CHECK(phase_ns->scalar_type() == at::kLong && phase_ns->is_cuda() && phase_ns->is_contiguous() &&
+                    phase_ns->numel() >= ((S + kBK - 1) / kBK) * heads * B * 8,
+                "phase_ns must be a CUDA int64 tensor of grid x 8 entries");
+    a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
+  }
   constexpr int smem = BwdSmem::total + 1024;
   static int configured_for = -1;
   int dev = 0;

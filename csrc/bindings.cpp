@@ -38,7 +38,7 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
 void scale_(torch::Tensor x, double s);
 // attention_tc.cu
 void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
-                 int64_t heads);
+                 int64_t heads, const c10::optional<torch::Tensor>& phase_ns);
 // comm.cu
 void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
                      const std::vector<int64_t>& shadow_ptrs, const std::vector<int64_t>& flag_ptrs, torch::Tensor m,
@@ -52,7 +52,8 @@ void ipc_close(int64_t base);
 std::vector<std::string> ipc_export(const torch::Tensor& t);
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
-                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum);
+                 int64_t S, int64_t heads, const c10::optional<torch::Tensor>& colsum,
+                 const c10::optional<torch::Tensor>& phase_ns);
 // embed_head.cu
 void bert_embed_fwd(const torch::Tensor& ids, const torch::Tensor& tt, const torch::Tensor& word,
                     const torch::Tensor& pos, const torch::Tensor& type, const torch::Tensor& gamma,
@@ -114,10 +115,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &revpp::attn_fwd, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"),
         py::arg("heads"));
   m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
-        py::arg("S"), py::arg("heads"));
+        py::arg("S"), py::arg("heads"), py::arg("phase_ns") = py::none());
   m.def("attn_bwd_tc", &revpp::attn_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
         py::arg("dqkv"), py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"),
-        py::arg("colsum") = py::none());
+        py::arg("colsum") = py::none(), py::arg("phase_ns") = py::none());
   m.def("attn_bwd", &revpp::attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("dqkv"),
         py::arg("dq_acc"), py::arg("D"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("bert_embed_fwd", &revpp::bert_embed_fwd);

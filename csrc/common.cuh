@@ -7,6 +7,8 @@
 // __trap() or device asserts.
 #pragma once
 
+#include <cstdio>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -88,9 +90,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
-// 2-D tiled load, no multicast.  x is the innermost coordinate (elements).
+// Debug builds (REVPP_DEBUG_BOUNDS=1, `REVPP_DEBUG_BOUNDS=1 python setup.py build_ext
+// --inplace`) check the innermost coordinate of every tiled TMA load before issuing it: on
+// sm_100a a start that is not 16-byte aligned is an illegal instruction that loses the
+// context.  A bad coordinate is printed and the copy skipped, so the consumer's bounded
+// mbarrier wait runs out and the kernel returns with an error status instead.
+#ifndef REVPP_DEBUG_BOUNDS
+#define REVPP_DEBUG_BOUNDS 0
+#endif
+__device__ __forceinline__ bool tma_coord_ok(int x, int elem_bytes) {
+  if constexpr (REVPP_DEBUG_BOUNDS) {
+    if ((x * elem_bytes) % 16 != 0) {
+      printf("revpp: TMA load skipped, innermost coordinate %d (%d-byte elements) is not 16-byte aligned\n", x,
+             elem_bytes);
+      return false;
+    }
+  }
+  return true;
+}
+
+// 2-D tiled load, no multicast.  x is the innermost coordinate (elements; every tensor map
+// of this project has 2-byte elements).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
+  if (!tma_coord_ok(x, 2)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
@@ -100,6 +123,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 // 3-D tiled load, no multicast.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int z) {
+  if (!tma_coord_ok(x, 2)) return;
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
           smem_u32(smem_dst)),
@@ -251,6 +275,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 // mbarrier at `mbar_cluster_addr` (the pair leader's), for 2-SM MMA.  No multicast.
 __device__ __forceinline__ void tma_load_2d_2sm(void* smem_dst, const CUtensorMap* map, uint32_t mbar_cluster_addr,
                                                 int x, int y) {
+  if (!tma_coord_ok(x, 2)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
       "%4}], [%2];" ::"r"(smem_u32(smem_dst)),

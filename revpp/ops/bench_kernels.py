@@ -96,6 +96,47 @@ def bench_attn(a, C, backward: bool):
             "tflops": 2.5 * flops / ms / 1e9}
 
 
+def attn_phases(a, C):
+    """Per-CTA phase times of the tcgen05 attention kernels (globaltimer stamps written by
+    the kernels when given a phase buffer): median time from the CTA's start to each
+    phase, the median CTA duration and the kernel span.  Forward phases: 1 Q and first K
+    landed, 2 first scores ready, 3 last P handed over, 4 merge starts, 5 merge done,
+    6 end.  Backward: 1 K, V, Q0, dO0 landed, 2 first S^T/dP^T ready, 3 last P^T/dS^T
+    handed over, 4 dK/dV complete, 5 dK written + column sums, 6 last dQ reduction read,
+    7 end."""
+    B, S, heads = a.B, a.S, a.heads
+    H = heads * 64
+    qkv = torch.randn(B * S, 3 * H, device="cuda").to(torch.bfloat16)
+    out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, heads, S, device="cuda")
+    res = {"op": "attn-phases", "B": B, "S": S, "heads": heads}
+    for kind in ("fwd", "bwd"):
+        grid = ((S + 127) // 128) * heads * B
+        ph = torch.zeros(grid * 8, dtype=torch.int64, device="cuda")
+        if kind == "fwd":
+            C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+            torch.cuda.synchronize()
+            C.attn_fwd_tc(qkv, out, lse, B, S, heads, phase_ns=ph)
+            nph = 7
+        else:
+            dout = torch.randn_like(out)
+            dqkv = torch.empty_like(qkv)
+            dq = torch.empty(B * S, H, device="cuda")
+            D = torch.empty(B, heads, S, device="cuda")
+            cs = torch.zeros(3 * H, device="cuda")
+            C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq, D, B, S, heads, colsum=cs)
+            torch.cuda.synchronize()
+            C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq, D, B, S, heads, colsum=cs, phase_ns=ph)
+            nph = 8
+        torch.cuda.synchronize()
+        t = ph.view(grid, 8)[:, :nph].double()
+        rel = (t - t[:, :1]) / 1e3  # us from the CTA's start
+        res[kind] = {"phase_us_median": [round(float(x), 2) for x in rel.median(0).values],
+                     "cta_us_median": round(float(rel[:, -1].median()), 2),
+                     "span_us": round(float((t[:, -1].max() - t[:, 0].min()) / 1e3), 2)}
+    return res
+
+
 def bench_layernorm(a, C):
     M, H = a.M, a.H
     x = torch.randn(M, H, device="cuda")
@@ -171,7 +212,7 @@ def layer_suite(a):
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "layernorm", "adamw", "suite"])
+    p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "attn-phases", "layernorm", "adamw", "suite"])
     p.add_argument("--M", type=int, default=16384)
     p.add_argument("--N", type=int, default=4096)
     p.add_argument("--K", type=int, default=1024)
@@ -203,6 +244,8 @@ def main(argv=None):
         r = bench_attn(a, C, False)
     elif a.op == "attn-bwd":
         r = bench_attn(a, C, True)
+    elif a.op == "attn-phases":
+        r = attn_phases(a, C)
     elif a.op == "layernorm":
         r = bench_layernorm(a, C)
     else:

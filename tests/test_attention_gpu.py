@@ -58,7 +58,8 @@ def test_attn_fwd_bwd(B, S, heads):
     assert C.status_read_and_clear() == 0
 
 
-@pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3), (1, 2048, 2)])
+@pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3), (1, 150, 2),
+                                       (1, 2048, 2)])
 def test_attn_fwd_tcgen05(B, S, heads):
     """tcgen05 forward against float64 attention and against the mma.sync kernel."""
     C = _C()
