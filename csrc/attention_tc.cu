@@ -482,6 +482,7 @@ struct BwdSmem {
   static constexpr uint32_t total = bars + 256;
 };
 static_assert(BwdSmem::total + 1024 <= 232448, "attention backward exceeds the shared-memory limit");
+static_assert(8 * 4096 + 4 * 128 * 4 <= 2 * kSqTile, "dK/dV staging and column sums must fit in the dS^T buffers");
 constexpr uint32_t kIdescSq = idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescKD = idesc_bf16(128, 64, false, true);
 constexpr uint32_t kIdescQD = idesc_bf16(128, 64, true, true);
@@ -817,8 +818,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // dK / dV complete in TMEM
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
-      const long long ld = 3LL * H;
-      const long long base = (static_cast<long long>(row0) + k0 + r) * ld + h * 64;
+      // The 64 columns of this warp's 32 key rows go through a 4 KB shared-memory tile
+      // (rows of 128 bytes, 16-byte units XOR-swizzled by row) in the dS^T buffers, which
+      // are free once kv_done has fired; the warp then stores 4 rows x 128 contiguous bytes
+      // per instruction instead of one 16-byte piece of 32 different rows.
+      uint8_t* stg = smem + BwdSmem::dst + (grp * 4 + quarter) * 4096;
+      float* red = reinterpret_cast<float*>(smem + BwdSmem::dst + 8 * 4096);  // column sums
       // dK (TMEM cols 320..383, scaled) or dV (256..319), 32 columns per load
 #pragma unroll 1
       for (int part = 2 * grp; part < 2 * grp + 2; ++part) {
@@ -832,12 +837,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * sc, __uint_as_float(v[2 * e + 1]) * sc);
-        const int gcol = (is_k ? H : 2 * H) + h * 64 + 32 * half;
-        if (key_ok) {
-          uint4* g = reinterpret_cast<uint4*>(args.dqkv + base - h * 64 + gcol);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) g[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + (((half * 4 + u) ^ (lane & 7)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         if (args.colsum != nullptr) {  // bias gradient of the K / V projections
           float cv[32];
 #pragma unroll
@@ -846,9 +849,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             cv[2 * e] = key_ok ? r2.x : 0.f;
             cv[2 * e + 1] = key_ok ? r2.y : 0.f;
           }
-          // this warp's 32 keys; the dS^T buffers are free once kv_done has fired
-          reinterpret_cast<float*>(smem + BwdSmem::dst)[quarter * 128 + part * 32 + lane] =
-              warp_column_sums32(cv, lane);
+          // this warp's 32 keys
+          red[quarter * 128 + part * 32 + lane] = warp_column_sums32(cv, lane);
+        }
+      }
+      __syncwarp();
+      {
+        const int u = lane & 7;
+        const long long gcol = (grp == 0 ? H : 2 * H) + h * 64 + u * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3);  // key row within this warp's 32
+          const int key = k0 + quarter * 32 + rr;
+          if (key < S) {
+            *reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + key) * (3LL * H) + gcol) =
+                *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
+          }
         }
       }
       if (args.colsum != nullptr) {
@@ -857,7 +873,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(cs_bar);
         if (grp == 0 && quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
-          const float* red = reinterpret_cast<const float*>(smem + BwdSmem::dst);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int c = i * 32 + lane;  // 0..63 dK columns, 64..127 dV columns
