@@ -61,14 +61,15 @@ struct AttnTcArgs {
   int S, heads;
   float scale_log2;
   int* status;
-  // optional [grid][8] globaltimer stamps of the CTA's phases (measurement aid)
+  // optional [grid][32] globaltimer stamps of the CTA's phases (measurement aid)
   unsigned long long* phase_ns = nullptr;
 };
 
+constexpr int kPhaseSlots = 32;  // per CTA: 8 phases, then per-tile events of the first 4 tiles
 __device__ __forceinline__ void phase_stamp(unsigned long long* ph, int k) {
   if (ph != nullptr) {
     const long long cta = blockIdx.x + static_cast<long long>(gridDim.x) * (blockIdx.y + static_cast<long long>(gridDim.y) * blockIdx.z);
-    ph[cta * 8 + k] = globaltimer_ns();
+    ph[cta * kPhaseSlots + k] = globaltimer_ns();
   }
 }
 
@@ -422,8 +423,8 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
   a.status = status_device_ptr();
   if (phase_ns.has_value() && phase_ns->defined()) {
     REVPP_CHECK(phase_ns->scalar_type() == at::kLong && phase_ns->is_cuda() && phase_ns->is_contiguous() &&
-                    phase_ns->numel() >= ((S + kQ - 1) / kQ) * heads * B * 8,
-                "phase_ns must be a CUDA int64 tensor of grid x 8 entries");
+                    phase_ns->numel() >= ((S + kQ - 1) / kQ) * heads * B * kPhaseSlots,
+                "phase_ns must be a CUDA int64 tensor of grid x 32 entries");
     a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
   }
   constexpr int smem = SmemLayout::total + 1024;
@@ -455,18 +456,22 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 //                        tile)                               -> TMEM cols [384, 448)
 //   dQ warps (one thread per query) stage dQ_j * scale in shared memory and add each
 //       256-byte row to an fp32 buffer with a bulk reduction (performed in L2).
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-63) / final dK, 6-9 dQ
-// and the LSE / D rows of the next query tile (double-buffered in smem, so the softmax
-// warps never wait for one another), 10-13 softmax (queries 64-127) / final dV.
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax (queries 0-31) / final dK, 6-9 dQ,
+// 10-13 softmax (queries 32-63) / final dV, 14-17 and
+// 18-21 softmax (queries 64-95, 96-127): four warps per scheduler share the exp / dS work
+// (with two, the per-tile softmax was latency-bound).
 // Overlap: as soon as the softmax of tile j has consumed S^T / dP^T, the issuer starts
-// S^T / dP^T of tile j+1 and only then the dV / dK / dQ MMAs of tile j, so the softmax of
-// tile j+1 runs while the tensor core works on tile j.  dS^T is therefore double-buffered
+// S^T / dP^T of tile j+1 (if its Q / dO rows have landed; else after this tile's MMAs) and
+// then the dV / dK / dQ MMAs of tile j, so the softmax of tile j+1 runs while the tensor
+// core works on tile j.  dS^T is therefore double-buffered
 // in shared memory; P^T (one TMEM buffer) is rewritten only after the previous tile's dV
 // MMAs have read it.
 namespace {
 constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
-constexpr int kBwdThreads = 448;
+constexpr int kBwdGroups = 4;                  // softmax groups, kQG queries of a tile each
+constexpr int kQG = 128 / kBwdGroups;
+constexpr int kBwdThreads = 64 + 128 + 32 * 4 * kBwdGroups;  // producer, MMA, dQ warps, softmax groups
 constexpr uint32_t kTile = 128 * 64 * 2;       // 16 KB: a [128 x 64] bf16 tile
 constexpr uint32_t kSqTile = 2 * kTile;        // 32 KB: a [128 x 128] bf16 tile (2 swizzle chunks)
 constexpr uint32_t kDqStride = 272;  // 256-byte dQ rows padded by 16: row r's chunk k is in bank group (r + k) % 8
@@ -476,8 +481,8 @@ struct BwdSmem {
   static constexpr uint32_t q = v + kTile;              // 2 buffers
   static constexpr uint32_t dout = q + 2 * kTile;       // 2 buffers
   static constexpr uint32_t dst = dout + 2 * kTile;     // dS^T, 2 buffers
-  static constexpr uint32_t stats = dst + 2 * kSqTile;  // 2 x {lse*log2e [128], D [128]}
-  static constexpr uint32_t dq = stats + 2 * 2 * 128 * 4;  // dQ_j fp32, 128 rows of 64, 272-byte stride
+  static constexpr uint32_t stats = dst + 2 * kSqTile;  // per softmax warp: lse*log2e [kQG], D [kQG]
+  static constexpr uint32_t dq = stats + 4 * kBwdGroups * 2 * kQG * 4;  // dQ_j fp32, 128 rows of 64, 272-byte stride
   static constexpr uint32_t bars = dq + 128 * kDqStride;
   static constexpr uint32_t total = bars + 256;
 };
@@ -499,7 +504,7 @@ struct AttnBwdTcArgs {
   float scale, scale_log2;
   int* status;
   float* colsum = nullptr;  // [3H] fp32 or null: += column sums of the bf16 dK / dV written here
-  unsigned long long* phase_ns = nullptr;  // optional [grid][8] globaltimer stamps (measurement aid)
+  unsigned long long* phase_ns = nullptr;  // optional [grid][32] globaltimer stamps (measurement aid)
 };
 
 // Column sums over the 32 rows (lanes) of a warp: v holds this lane's 32 columns; returns
@@ -540,10 +545,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* cs_bar = bar + 16;    // the eight dK / dV warps' column sums are in shared memory
   uint64_t* pt_free = bar + 17;   // the dV MMAs of a tile have read P^T from TMEM
-  uint64_t* st_full = bar + 18;   // [2] LSE / D rows of a query tile staged
-  uint64_t* st_empty = bar + 20;  // [2] the eight softmax warps are done with them
   uint64_t* s_free = bar + 22;    // the eight softmax warps have read S^T / dP^T of a tile
-  float* s_stats = reinterpret_cast<float*>(smem + BwdSmem::stats);  // [2][256]: lse*log2e, D
+  float* s_stats = reinterpret_cast<float*>(smem + BwdSmem::stats);  // [softmax warp][2 kQG]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -562,7 +565,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 8);
+    mbar_init(p_full, 4 * kBwdGroups);
     mbar_init(&p_empty[0], 1);
     mbar_init(&p_empty[1], 1);
     mbar_init(dq_full, 1);
@@ -572,11 +575,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(grp_bar, 8);
     mbar_init(cs_bar, 8);
     mbar_init(pt_free, 1);
-    mbar_init(s_free, 8);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&st_full[i], 4);
-      mbar_init(&st_empty[i], 8);
-    }
+    mbar_init(s_free, 4 * kBwdGroups);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -660,16 +659,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // so its scores are computed while they finish tile j and its softmax overlaps
         // this tile's gradient MMAs
         if (!mbar_wait(s_free, jp, args.status, abort_flag)) break;
+        if (j < 4) phase_stamp(args.phase_ns, 8 + 4 * j + 2);  // tile j's scores read
         tc_fence_after();
-        if (j + 1 < nq) {
-          if (!mbar_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status, abort_flag)) break;
+        // S of tile j+1 goes first if its Q / dO rows have landed; otherwise this tile's
+        // gradient MMAs go first, so they (and the release of this tile's Q / dO buffer,
+        // which the load of tile j+2 waits for) never wait on the load of tile j+1
+        bool s_next = false;
+        if (j + 1 < nq && mbar_try_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
           tc_fence_after();
           issue_s(j + 1);
+          s_next = true;
         }
         // softmax of tile j is done: P^T of tile j is in TMEM, dS^T in buffer pb
         if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
         tc_fence_after();
         if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
+        if (j < 4) phase_stamp(args.phase_ns, 8 + 4 * j + 3);  // tile j's gradient MMAs issued
         tc_fence_after();
         const uint32_t a_dsj = a_ds + pb * kSqTile;
 #pragma unroll
@@ -697,6 +702,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(dq_full);
         umma_commit(&p_empty[pb]);
         umma_commit(&q_empty[bb]);
+        if (j + 1 < nq && !s_next) {
+          if (!mbar_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status, abort_flag)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
       }
       umma_commit(kv_done);
       umma_commit(drain);
@@ -706,29 +716,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp < 6 || warp >= 10) {
     // ------------------------------------------------------------------ softmax (keys)
-    // Two warpgroups: warps 2-5 take queries [0, 64) of the tile, warps 10-13 [64, 128);
-    // each warp owns the 32 TMEM lanes (keys) of its quarter.
-    const int grp = warp >= 10 ? 1 : 0;
+    // kBwdGroups warpgroups: warps 2-5 take queries [0, kQG) of the tile, warps 10-13 the
+    // next kQG, and so on; each warp owns the 32 TMEM lanes (keys) of its quarter.
+    const int grp = warp < 6 ? 0 : (warp - 10) / 4 + 1;
+    const int qb = grp * kQG;               // first query of this group within the tile
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;      // key row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const bool key_ok = k0 + r < S;
     uint8_t* ds_base = smem + BwdSmem::dst;
+    // Every softmax warp keeps its own copy of the LSE (log2 units; +inf past the sequence
+    // end, so P = 0 there) and D of its group's kQG queries, fetched into registers one
+    // tile ahead (lane l holds query qb + l): no warp waits for another's staging.
+    float* wst = s_stats + (grp * 4 + quarter) * 2 * kQG;
+    const float4* s_lse4 = reinterpret_cast<const float4*>(wst);
+    const float4* s_D4 = reinterpret_cast<const float4*>(wst + kQG);
+    auto fetch_stats = [&](int t, float& l2, float& dd) {
+      const int q = t * kBQ + qb + lane;
+      l2 = q < S ? g_lse[q] * 1.4426950408889634f : __int_as_float(0x7f800000);
+      dd = q < S ? g_D[q] : 0.f;
+    };
+    float nl2 = 0.f, ndd = 0.f;
+    if (nq > 0) fetch_stats(0, nl2, ndd);
     bool ok = true;
     for (int j = 0; j < nq; ++j) {
       const uint32_t jp = j & 1;
       const uint32_t pb = j & 1;
-      const float4* s_lse4 = reinterpret_cast<const float4*>(s_stats + pb * 256);
-      const float4* s_D4 = s_lse4 + 32;
-      if (!mbar_wait(&st_full[pb], (j >> 1) & 1, args.status, abort_flag)) {
-        ok = false;
-        break;
-      }
+      __syncwarp();  // this warp's reads of the previous tile's stats are done
+      wst[lane] = nl2;
+      wst[kQG + lane] = ndd;
+      __syncwarp();
+      if (j + 1 < nq) fetch_stats(j + 1, nl2, ndd);
       if (!mbar_wait(s_full, jp, args.status, abort_flag)) {
         ok = false;
         break;
       }
       if (j == 0 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 2);  // first S^T / dP^T ready
+      if (j < 4 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 8 + 4 * j + 0);  // tile j: softmax starts
       if (!mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) {
         ok = false;
         break;
@@ -741,82 +765,72 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       const int sw = r & 7;
-      // this group's 64 queries are 64-query swizzle chunk `grp` of the dS^T tile
-      uint8_t* drow = ds_base + pb * kSqTile + grp * kTile + (r >> 3) * 1024 + sw * 128;
+      // the dS^T tile is two 64-query swizzle chunks; this group's queries start at 16-byte
+      // unit (qb % 64) / 8 of chunk qb / 64
+      uint8_t* drow = ds_base + pb * kSqTile + (qb / 64) * kTile + (r >> 3) * 1024 + sw * 128;
+      const int u0 = (qb % 64) / 8;
       const float sl2 = args.scale_log2;
-      // Four 16-query sub-chunks, software-pipelined: the S^T / dP^T columns of sub-chunk
-      // k + 1 are loaded from TMEM while sub-chunk k is computed.
-      uint32_t sv[2][16], dp[2][16];
-      tmem_ld16(tmem + lane_off + grp * 64, sv[0]);
-      tmem_ld16(tmem + lane_off + 128 + grp * 64, dp[0]);
-      tmem_wait_ld();
-      tmem_regs_ready(sv[0]);
-      tmem_regs_ready(dp[0]);
+      // kQG / 16 sub-chunks of 16 queries (latency is hidden by the other groups' warps)
+      constexpr int KS = kQG / 16;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int cur = k & 1;
-        if (k < 3) {
-          tmem_ld16(tmem + lane_off + grp * 64 + 16 * (k + 1), sv[cur ^ 1]);
-          tmem_ld16(tmem + lane_off + 128 + grp * 64 + 16 * (k + 1), dp[cur ^ 1]);
+      for (int k = 0; k < KS; ++k) {
+        uint32_t sv[16], dp[16];
+        tmem_ld16(tmem + lane_off + qb + 16 * k, sv);
+        tmem_ld16(tmem + lane_off + 128 + qb + 16 * k, dp);
+        tmem_wait_ld();
+        if (k == KS - 1) {  // every S^T / dP^T column of this tile is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_free);
         }
-        const int q4 = (grp * 64 + 16 * k) / 4;  // first float4 of this sub-chunk's LSE / D
+        const int q4 = 4 * k;  // first float4 of this sub-chunk's LSE / D in the warp's copy
         uint32_t pw[8], dw[8];
         if (key_ok) {
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
             const float4 L = s_lse4[q4 + e4];
             const float4 Dq = s_D4[q4 + e4];
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 0]), sl2, -L.x));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 1]), sl2, -L.y));
-            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 2]), sl2, -L.z));
-            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[cur][4 * e4 + 3]), sl2, -L.w));
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 0]), sl2, -L.x));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 1]), sl2, -L.y));
+            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 2]), sl2, -L.z));
+            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 3]), sl2, -L.w));
             const uint32_t pp0 = pack_bf16x2(p0, p1), pp1 = pack_bf16x2(p2, p3);
             const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
             pw[2 * e4] = pp0;
             pw[2 * e4 + 1] = pp1;
-            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[cur][4 * e4 + 0]) - Dq.x),
-                                     r0.y * (__uint_as_float(dp[cur][4 * e4 + 1]) - Dq.y));
-            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[cur][4 * e4 + 2]) - Dq.z),
-                                         r1.y * (__uint_as_float(dp[cur][4 * e4 + 3]) - Dq.w));
+            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[4 * e4 + 0]) - Dq.x),
+                                     r0.y * (__uint_as_float(dp[4 * e4 + 1]) - Dq.y));
+            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[4 * e4 + 2]) - Dq.z),
+                                         r1.y * (__uint_as_float(dp[4 * e4 + 3]) - Dq.w));
           }
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) pw[e] = dw[e] = 0u;
         }
-        // P^T: the 16 queries are TMEM columns kTmemPt + 32 grp + 8k .. + 7 of this key's lane
-        tmem_st8(tmem + lane_off + kTmemPt + 32 * grp + 8 * k, pw);
-        // dS^T: 16 queries = 32 bytes = 16-byte units 2k, 2k + 1 of this group's row
+        // P^T: the 16 queries are TMEM columns kTmemPt + (qb + 16k) / 2 .. + 7 of this key's lane
+        tmem_st8(tmem + lane_off + kTmemPt + qb / 2 + 8 * k, pw);
+        // dS^T: 16 queries = 32 bytes = 16-byte units u0 + 2k, u0 + 2k + 1 of this row
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          const uint32_t off = ((2 * k + t) ^ sw) << 4;
+          const uint32_t off = ((u0 + 2 * k + t) ^ sw) << 4;
           *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
         }
-        if (k < 3) {
-          tmem_wait_ld();
-          tmem_regs_ready(sv[cur ^ 1]);
-          tmem_regs_ready(dp[cur ^ 1]);
-          if (k == 2) {  // every S^T / dP^T column of this tile is in registers
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
-          }
-        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&st_empty[pb]);  // this warp is done with the tile's LSE / D
       tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (j < 4 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 8 + 4 * j + 1);  // tile j: handed over
     }
     // final dK (group 0) and dV (group 1) for this warp's keys; the decision is made
     // warp-uniform since the column sums below shuffle across all lanes
     if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 3);  // last tile's P^T / dS^T handed over
-    bool fin = ok;
+    // (groups 2 and up have no write-out)
+    bool fin = ok && grp < 2;
     if (fin) fin = mbar_wait(kv_done, 0, args.status, abort_flag);
     if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // dK / dV complete in TMEM
-    if (__all_sync(0xffffffffu, fin)) {
+    if (grp < 2 && __all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       // The 64 columns of this warp's 32 key rows go through a 4 KB shared-memory tile
       // (rows of 128 bytes, 16-byte units XOR-swizzled by row) in the dS^T buffers, which
@@ -888,21 +902,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    // LSE (log2 units; +inf past the sequence end, so P = 0 there) and D of query tile t
-    // into stats buffer t & 1, once the softmax warps are done with tile t - 2
-    auto stage_stats = [&](int t) -> bool {
-      const int sb = t & 1;
-      if (t >= 2 && !mbar_wait(&st_empty[sb], ((t >> 1) & 1) ^ 1u, args.status, abort_flag)) return false;
-      const int q = t * kBQ + r;
-      s_stats[sb * 256 + r] = q < S ? g_lse[q] * 1.4426950408889634f : __int_as_float(0x7f800000);
-      s_stats[sb * 256 + 128 + r] = q < S ? g_D[q] : 0.f;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&st_full[sb]);
-      return true;
-    };
-    bool sok = nq < 1 || stage_stats(0);
     for (int j = 0; j < nq; ++j) {
-      if (sok && j + 1 < nq) sok = stage_stats(j + 1);
       if (!mbar_wait(dq_full, j & 1, args.status, abort_flag)) break;
       tc_fence_after();
       uint32_t dq[2][32];
@@ -1048,8 +1048,8 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   a.colsum = cs;
   if (phase_ns.has_value() && phase_ns->defined()) {
     REVPP_CHECK(phase_ns->scalar_type() == at::kLong && phase_ns->is_cuda() && phase_ns->is_contiguous() &&
-                    phase_ns->numel() >= ((S + kBK - 1) / kBK) * heads * B * 8,
-                "phase_ns must be a CUDA int64 tensor of grid x 8 entries");
+                    phase_ns->numel() >= ((S + kBK - 1) / kBK) * heads * B * kPhaseSlots,
+                "phase_ns must be a CUDA int64 tensor of grid x 32 entries");
     a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
   }
   constexpr int smem = BwdSmem::total + 1024;

@@ -112,7 +112,7 @@ def attn_phases(a, C):
     res = {"op": "attn-phases", "B": B, "S": S, "heads": heads}
     for kind in ("fwd", "bwd"):
         grid = ((S + 127) // 128) * heads * B
-        ph = torch.zeros(grid * 8, dtype=torch.int64, device="cuda")
+        ph = torch.zeros(grid * 32, dtype=torch.int64, device="cuda")
         if kind == "fwd":
             C.attn_fwd_tc(qkv, out, lse, B, S, heads)
             torch.cuda.synchronize()
@@ -129,11 +129,17 @@ def attn_phases(a, C):
             C.attn_bwd_tc(qkv, out, dout, lse, dqkv, dq, D, B, S, heads, colsum=cs, phase_ns=ph)
             nph = 8
         torch.cuda.synchronize()
-        t = ph.view(grid, 8)[:, :nph].double()
+        full = ph.view(grid, 32).double()
+        t = full[:, :nph]
         rel = (t - t[:, :1]) / 1e3  # us from the CTA's start
         res[kind] = {"phase_us_median": [round(float(x), 2) for x in rel.median(0).values],
                      "cta_us_median": round(float(rel[:, -1].median()), 2),
                      "span_us": round(float((t[:, -1].max() - t[:, 0].min()) / 1e3), 2)}
+        if kind == "bwd":  # per query tile: softmax start, hand-over, next S issued, gradient MMAs issued
+            nt = min(4, (S + 127) // 128)
+            tiles = (full[:, 8:8 + 4 * nt] - full[:, :1]) / 1e3
+            med = [round(float(x), 2) for x in tiles.median(0).values]
+            res[kind]["tiles_us_median"] = [med[4 * i:4 * i + 4] for i in range(nt)]
     return res
 
 
