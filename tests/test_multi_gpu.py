@@ -32,8 +32,9 @@ def _run(mode, n=2, timeout=240):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", REVPP_MGPU_RESULT_DIR=res_dir)
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
     if p.returncode != 0:
-        out_dir = os.path.join(os.environ.get("GRAFT_REPO_ROOT", os.path.dirname(HERE)), "gpurun_out")
-        if os.path.isdir(out_dir):
+        # full worker output for post-mortems when REVPP_TEST_LOG_DIR names an existing folder
+        out_dir = os.environ.get("REVPP_TEST_LOG_DIR")
+        if out_dir and os.path.isdir(out_dir):
             with open(os.path.join(out_dir, f"mgpu_{mode}_fail.log"), "w") as fh:
                 fh.write(p.stdout + "\n----- stderr -----\n" + p.stderr)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
