@@ -304,8 +304,11 @@ def run_reference(args):
 
     def step(i):
         # the loop body of the reference Engine (BERT/src/engine.py:160-281); its own loop
-        # deletes an unbound name after the first batch on rank 0 (engine.py:197).
+        # deletes an unbound name after the first batch on rank 0 (engine.py:197).  Returns
+        # the batch loss on the last rank: the reference's 1F1B turns every micro-batch loss
+        # into a host float (loss.item(), schedules.py:778-784), and the engine averages them.
         b = host[i % 2]
+        loss = None
         if rank == 0:
             ids = b["ids"].to(dev, non_blocking=True)
             mask = b["mask"].to(dev, non_blocking=True)
@@ -316,6 +319,7 @@ def run_reference(args):
             dist.irecv(labels_buf, src=0).wait()
             losses = []
             sched.step(target=labels_buf, losses=losses)
+            loss = sum(losses) / len(losses)
         else:
             sched.step()
         for p in model.parameters():
@@ -324,6 +328,7 @@ def run_reference(args):
         torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
         opt.step()
         opt.zero_grad()
+        return loss
 
     for i in range(args.warmup):
         step(i)
@@ -343,9 +348,31 @@ def run_reference(args):
     barrier(dev)
     ms_max = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     peak = max_over_ranks(torch.cuda.max_memory_allocated() / 2**30, dev)
+
+    # ---- end-to-end, measured as the revpp arm measures it: each step's inputs go host ->
+    # device from pinned memory inside the step (rank 0), the batch loss reaches the host
+    # (the reference reads every micro-batch loss with .item()), wall clock, max over ranks
+    e2e = None
+    if not args.no_e2e:
+        h2d = sum(t.numel() * t.element_size() for t in host[0].values()) if rank == 0 else 0
+        barrier(dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            loss = step(i)
+            if loss is not None:
+                float(loss)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3 / args.steps
+        barrier(dev)
+        wall_max = max_over_ranks(wall, dev)
+        h2d_total = sum_over_ranks(float(h2d), dev)
+        e2e = {"value": args.global_batch / (wall_max / 1e3), "unit": "samples/s", "ms_per_step": wall_max,
+               "h2d_bytes_per_step": int(h2d_total), "d2h_bytes_per_step": 4 * nmb,
+               "api": "pipelining.Schedule1F1B.step (reference Engine loop body)"}
     rec = base_record(args, world, "reference")
-    rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "peak_hbm_gib": peak,
-                "clocks": clocks, "gpu_launches": 0,
+    rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "e2e": e2e,
+                "peak_hbm_gib": peak, "clocks": clocks, "gpu_launches": 0,
                 "api": "pipelining.RevPipelineStageWithPareprop + Schedule1F1B (baseline/_ref/BERT)"})
     if rank == 0:
         print(json.dumps(rec), flush=True)

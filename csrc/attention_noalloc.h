@@ -26,11 +26,14 @@
 // them) race and give wrong results.  The entry point clears the part of the scratch that
 // must start at zero itself, so sequential calls are independent.
 //
-// `status` (optional, device int): bits set by the kernels if a bounded wait inside them
-// gave up (1 = mbarrier wait).  With `status == NULL` they go to a word inside the scratch
-// array.  `stream` is a cudaStream_t (NULL = legacy default stream).  `err` (optional)
-// receives a message of at most `errlen` bytes, NUL-terminated, when the return value is
-// not REVPP_NOALLOC_OK.
+// `status` (device int, strongly recommended): bits set by the kernels if a bounded wait
+// inside them gave up (1 = mbarrier wait); the output is then incomplete.  The caller
+// clears the word before the call and reads it after synchronising the stream.  With
+// `status == NULL` the bits go to a word inside the scratch array that no caller can read,
+// and the return value (which is known before the kernels run) is still REVPP_NOALLOC_OK:
+// a caller that passes NULL cannot detect such a failure.  `stream` is a cudaStream_t
+// (NULL = legacy default stream).  `err` (optional) receives a message of at most `errlen`
+// bytes, NUL-terminated, when the return value is not REVPP_NOALLOC_OK.
 #ifndef REVPP_ATTENTION_NOALLOC_H_
 #define REVPP_ATTENTION_NOALLOC_H_
 

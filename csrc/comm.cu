@@ -16,7 +16,10 @@
 //   D. second flag barrier: no rank leaves until every peer's parameter stores are visible.
 // Traffic per rank: (D-1)/D of the gradient in, (D-1)/D of the parameters (fp32 + bf16)
 // out, no intermediate copies.  No TMA is used here, so no multicast load can touch peer
-// memory.  Every wait gives up after `timeout_ns`, records kStatusFlagTimeout and returns.
+// memory.  Every wait gives up after `timeout_ns`, records kStatusFlagTimeout, writes an
+// abort mark into every replica's flag page (so peers still waiting, or about to start
+// step C, skip the update instead of leaving the replicas with mixed old and new shards)
+// and returns; the trainer raises on the status bit at the end of the step.
 //
 // flag_wait_probe: a one-thread kernel that waits on a flag nobody sets, used by tests to
 // check that the bounded wait reports an error instead of hanging.
@@ -34,9 +37,11 @@ namespace cg = cooperative_groups;
 namespace revpp {
 
 constexpr int kMaxPeers = 8;
-// flag page layout (int32 words): [0, 64) epoch flags per rank, [64, 128) norm bits per rank
+// flag page layout (int32 words): [0, 64) epoch flags per rank, [64, 72) norm bits per rank,
+// word 127 the abort mark (the epoch base of the next call, written by a rank that gave up)
 constexpr int kFlagEpoch = 0;
 constexpr int kFlagNorm = 64;
+constexpr int kFlagAbort = 127;
 constexpr int kFlagWords = 128;
 
 struct DpArgs {
@@ -57,13 +62,33 @@ struct DpArgs {
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 __device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
-// Wait until flags[idx(d)] >= epoch for every rank d (in our own page).  Returns false on timeout.
-__device__ bool wait_all_flags(int* own_flags, int D, int epoch, long long timeout_ns, int* status) {
+// True once some rank has marked this call (epoch base `base`) as aborted in our page.
+__device__ __forceinline__ bool aborted(const int* own_flags, int base) {
+  return ld_volatile(own_flags + kFlagAbort) > base;
+}
+
+// Mark the call aborted in every replica's page (best effort: a peer that is already past
+// its last check completes the update, and the host-side status check fails the step).
+__device__ void raise_abort(const DpArgs& a, int base) {
+  __threadfence_system();
+  for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagAbort, base + 3);
+  __threadfence_system();
+}
+
+// Wait until flags[idx(d)] >= epoch for every rank d (in our own page).  Returns false on
+// timeout (after raising the abort mark in every page) or when a peer raised it.
+__device__ bool wait_all_flags(const DpArgs& a, int epoch, int base) {
+  const int* own = a.flags[a.rank];
   const uint64_t t0 = globaltimer_ns();
-  for (int d = 0; d < D; ++d) {
-    while (ld_volatile(own_flags + kFlagEpoch + d) < epoch) {
-      if (globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
-        atomicOr(status, kStatusFlagTimeout);
+  for (int d = 0; d < a.D; ++d) {
+    while (ld_volatile(own + kFlagEpoch + d) < epoch) {
+      if (aborted(own, base)) {
+        atomicOr(a.status, kStatusFlagTimeout);
+        return false;
+      }
+      if (globaltimer_ns() - t0 > static_cast<uint64_t>(a.timeout_ns)) {
+        atomicOr(a.status, kStatusFlagTimeout);
+        raise_abort(a, base);
         return false;
       }
       __nanosleep(256);
@@ -88,7 +113,7 @@ __global__ void __launch_bounds__(512, 2) dp_reduce_adamw_kernel(DpArgs a) {
     a.sumsq_scratch[0] = 0.f;
     __threadfence_system();
     for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 1);
-    a.sumsq_scratch[1] = wait_all_flags(a.flags[a.rank], a.D, base + 1, a.timeout_ns, a.status) ? 1.f : -1.f;
+    a.sumsq_scratch[1] = wait_all_flags(a, base + 1, base) ? 1.f : -1.f;
   }
   grid.sync();
   if (reinterpret_cast<volatile float*>(a.sumsq_scratch)[1] < 0.f) return;
@@ -144,7 +169,12 @@ __global__ void __launch_bounds__(512, 2) dp_reduce_adamw_kernel(DpArgs a) {
     for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagNorm + a.rank, __float_as_int(mine));
     __threadfence_system();
     for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 2);
-    int ok = wait_all_flags(a.flags[a.rank], a.D, base + 2, a.timeout_ns, a.status) ? 1 : 0;
+    int ok = wait_all_flags(a, base + 2, base) ? 1 : 0;
+    // a peer that gave up at barrier 0 or 1 skips its update: then nobody updates
+    if (ok && aborted(a.flags[a.rank], base)) {
+      atomicOr(a.status, kStatusFlagTimeout);
+      ok = 0;
+    }
     float total = 0.f;
     for (int d = 0; d < a.D; ++d) total += __int_as_float(ld_volatile(a.flags[a.rank] + kFlagNorm + d));
     float coef = 1.f;
@@ -215,7 +245,7 @@ __global__ void __launch_bounds__(512, 2) dp_reduce_adamw_kernel(DpArgs a) {
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     __threadfence_system();
     for (int d = 0; d < a.D; ++d) st_volatile(a.flags[d] + kFlagEpoch + a.rank, base + 3);
-    wait_all_flags(a.flags[a.rank], a.D, base + 3, a.timeout_ns, a.status);
+    wait_all_flags(a, base + 3, base);
   }
 }
 

@@ -214,8 +214,8 @@ def build_loaders(cfg: GlobalConfig, rank: int, world: int, num_stages: int, dev
         nt, nv = len(train), len(val)
     if dist.is_initialized() and cfg.par_mode == ParMode.PP:
         t = torch.tensor([nt, nv], dtype=torch.int64, device=device)
-        src = (rank // num_stages) * num_stages
-        # every pipeline's first stage holds the counts; replicas agree by construction
+        # every pipeline's first stage holds the counts and the replicas agree by construction,
+        # so global rank 0 (the first stage of replica 0) speaks for all of them
         dist.broadcast(t, src=0)
         nt, nv = int(t[0]), int(t[1])
     return LoaderBundle(train, val, nt, nv, local_batch)

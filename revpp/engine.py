@@ -44,6 +44,10 @@ from revpp.utils.env import EnvContext
 from revpp.utils.profiling import annotate
 
 
+class DeviceWaitError(RuntimeError):
+    """A kernel's bounded wait ran out of time (recorded in the device status word)."""
+
+
 def layout(cfg: GlobalConfig, world: int):
     if cfg.par_mode == ParMode.PP:
         return world // cfg.dp, cfg.dp
@@ -80,6 +84,7 @@ class Trainer:
         lowp = cfg.autocast_dtype == torch.bfloat16 and self.device.type == "cuda"
         self.flat = FlatParams(self.module, self.device, want_shadow=lowp)
         self.math = make_math(self.flat, cfg.autocast_dtype, cfg.num_attention_heads, self.device)
+        self.uses_kernels = self.device.type == "cuda"
         self.eh = make_embed_head(self.module, self.flat, cfg.autocast_dtype, self.device)
         kind = runtime_kind(cfg)
         self.stage = STAGE_TYPES[kind](self.module, self.math, self.eh, self.mbs, cfg.num_microbatches, self.device,
@@ -167,7 +172,29 @@ class Trainer:
         return None
 
     def finish_step(self) -> None:
-        """Replica gradient reduction, clipping and the optimizer update."""
+        """Replica gradient reduction, clipping and the optimizer update, then a check of the
+        device status word."""
+        self._update()
+        self.check_device_status()
+
+    def check_device_status(self, sync: bool = False) -> None:
+        """Raise if a bounded wait inside one of the extension's kernels gave up (its output
+        is then incomplete: an mbarrier wait in a tensor-core kernel, or a peer flag in the
+        fused replica all-reduce).  The word lives in mapped host memory, so the read costs
+        no device synchronisation; a failure in a kernel still running is seen by a later
+        check (``sync=True`` waits for the device first)."""
+        if not self.uses_kernels:
+            return
+        from revpp import ops
+
+        if sync:
+            torch.cuda.synchronize(self.device)
+        st = ops.check_status(clear=False)
+        if st:
+            raise DeviceWaitError(f"rank {self.rank}: device status word {st:#x} after step {self.step_count} "
+                                  "(a bounded wait inside a kernel gave up; results of this step are incomplete)")
+
+    def _update(self) -> None:
         if self.dp_reducer is not None:
             with annotate("## dp_allreduce ##"):
                 if self.dp_reducer.fused_update:
@@ -211,6 +238,7 @@ class Trainer:
             self.comms.drain()
         if self.dp_reducer is not None and hasattr(self.dp_reducer, "close"):
             self.dp_reducer.close()
+        self.check_device_status(sync=True)
 
 
 @dataclass

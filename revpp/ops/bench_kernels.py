@@ -63,8 +63,15 @@ def bench_gemm(a, C):
         resid = torch.randn(M, N, device=dev) if epi == 2 else None
         fn = lambda: C.gemm_tc(A, False, B, False, M, N, K, epi, out, bias=bias, aux_out=aux,  # noqa: E731
                                resid=resid, variant=a.variant)
+    if a.cublas:  # the same product through cuBLAS (torch.matmul, bf16 out), for comparison
+        if a.layout == "wgrad":
+            fn = lambda: torch.matmul(A.t(), B)  # noqa: E731
+        elif a.layout == "dgrad":
+            fn = lambda: torch.matmul(A, B)  # noqa: E731
+        else:
+            fn = lambda: torch.matmul(A, B.t())  # noqa: E731
     ms = _time(fn, a.warmup, a.iters)
-    return {"op": "gemm", "layout": a.layout, "epi": a.epi, "variant": a.variant, "M": M, "N": N, "K": K,
+    return {"op": "gemm" + ("-cublas" if a.cublas else ""), "layout": a.layout, "epi": a.epi, "variant": a.variant, "M": M, "N": N, "K": K,
             "colsum": bool(a.colsum), "aux_out": a.epi == "gelu" and not a.no_aux_out,
             "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9}
 
@@ -232,6 +239,7 @@ def main(argv=None):
     p.add_argument("--S", type=int, default=512)
     p.add_argument("--heads", type=int, default=16)
     p.add_argument("--impl", choices=["tc", "mma"], default="tc")
+    p.add_argument("--cublas", action="store_true", help="gemm: time torch.matmul on the same shape instead")
     p.add_argument("--n", type=int, default=335_000_000)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=20)
@@ -242,7 +250,9 @@ def main(argv=None):
     if a.op == "suite":
         extra = ["--warmup", str(a.warmup), "--iters", str(a.iters)]
         for args in layer_suite(a):
-            main(args + extra)
+            if a.cublas and args[0] != "gemm":
+                continue
+            main(args + extra + (["--cublas"] if a.cublas else []))
         return
     if a.op == "gemm":
         r = bench_gemm(a, C)

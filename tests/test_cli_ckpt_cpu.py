@@ -164,19 +164,3 @@ def test_bench_paber_microbatch_default(monkeypatch):
         a = bench.parse()
         assert a.microbatch_size == want, (argv, a.microbatch_size)
         assert a.global_batch % (a.microbatch_size * a.dp) == 0
-
-
-def test_bench_paber_microbatch_default(monkeypatch):
-    """bench.py picks the expanded micro-batch on a single stage and 16 with a pipeline,
-    and an explicit --microbatch-size wins."""
-    import importlib.util
-
-    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
-    bench = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(bench)
-    for argv, want in ((["--gpus", "1"], 64), (["--gpus", "2"], 16), (["--gpus", "8"], 16),
-                       (["--gpus", "2", "--dp", "2"], 64), (["--gpus", "1", "--microbatch-size", "32"], 32)):
-        monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
-        a = bench.parse()
-        assert a.microbatch_size == want, (argv, a.microbatch_size)
-        assert a.global_batch % (a.microbatch_size * a.dp) == 0

@@ -6,6 +6,7 @@ import socket
 import time
 
 import pytest
+import torch
 import torch.multiprocessing as mp
 
 
@@ -92,3 +93,28 @@ def test_rank_exit_peer_fails():
     assert 0 not in res or res[0] != "ok"
     assert res.get(1, "").startswith("error"), res
     assert dt < 80
+
+
+def test_trainer_checks_device_status_word(monkeypatch):
+    """finish_step reads the device status word and raises on any set bit (a fake read here;
+    the GPU test sets a real bit with a timed-out flag wait)."""
+    import revpp.ops as ops
+    from revpp.config import GlobalConfig
+    from revpp.engine import DeviceWaitError, Trainer
+    from revpp.utils.env import EnvContext
+    from revpp.utils.logger import build_logger
+
+    cfg = GlobalConfig(model="bert", reversible=True, num_hidden_layers=1, hidden_size=32, num_attention_heads=2,
+                       max_position_embeddings=16, num_classes=2, autocast_dtype=torch.float32, batch_size=4,
+                       microbatch_size=2, num_microbatches=2, lr=1e-4)
+    env = EnvContext(world_size=1, rank=0, local_rank=0, device=torch.device("cpu"),
+                     proc_logger=build_logger("st", None), node_logger=None, main_logger=None, pg=None,
+                     master_rank=0)
+    tr = Trainer(cfg, env)
+    tr.uses_kernels = True
+    word = {"v": 0}
+    monkeypatch.setattr(ops, "check_status", lambda clear=True: word["v"])
+    tr.check_device_status()  # clean word: no error
+    word["v"] = 1
+    with pytest.raises(DeviceWaitError):
+        tr.check_device_status()
