@@ -49,6 +49,7 @@ void flag_wait_probe(torch::Tensor flag, int64_t expect, double timeout_s, torch
 std::vector<int64_t> pointer_info(int64_t ptr);
 int64_t ipc_open(const std::string& handle_bytes);
 void ipc_close(int64_t base);
+void copy_to_ptr(int64_t dst, const torch::Tensor& src);
 std::vector<std::string> ipc_export(const torch::Tensor& t);
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch::Tensor& dout,
                  const torch::Tensor& lse, torch::Tensor dqkv, torch::Tensor dq_acc, torch::Tensor Dbuf, int64_t B,
@@ -140,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pointer_info", &revpp::pointer_info);
   m.def("ipc_open", [](py::bytes h) { return revpp::ipc_open(std::string(h)); });
   m.def("ipc_close", &revpp::ipc_close);
+  m.def("copy_to_ptr", &revpp::copy_to_ptr, "cudaMemcpyAsync of a contiguous tensor to a device address (a peer's IPC-mapped slot) on the current stream", py::arg("dst"), py::arg("src"));
   m.def("ipc_export", [](const torch::Tensor& t) {
     auto v = revpp::ipc_export(t);
     return py::make_tuple(py::bytes(v[0]), std::stoll(v[1]));

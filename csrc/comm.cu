@@ -352,6 +352,17 @@ int64_t ipc_open(const std::string& handle_bytes) {
 
 void ipc_close(int64_t base) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(base)); }
 
+// Copy a contiguous CUDA tensor to a device address on the current stream.  For an address
+// in a peer GPU's IPC-mapped memory this is a copy-engine transfer over NVLink: it uses no
+// SMs, so it overlaps the kernels of both GPUs (the pipeline's stage-to-stage messages).
+void copy_to_ptr(int64_t dst, const torch::Tensor& src) {
+  REVPP_CHECK(src.is_cuda() && src.is_contiguous(), "copy_to_ptr needs a contiguous CUDA tensor");
+  REVPP_CHECK(dst != 0 && (dst & 15) == 0, "destination must be a 16-byte aligned device address");
+  c10::cuda::CUDAGuard guard(src.device());
+  REVPP_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<void*>(dst), src.data_ptr(), src.nbytes(),
+                                   cudaMemcpyDeviceToDevice, cur_stream()));
+}
+
 // IPC handle bytes and byte offset of the allocation containing `t`'s data.
 std::vector<std::string> ipc_export(const torch::Tensor& t) {
   REVPP_CHECK(t.is_cuda(), "IPC export needs a CUDA tensor");

@@ -60,6 +60,8 @@ class GlobalConfig:
     inverse: bool = False
     checkpointing: bool = False
     schedule: str = "1f1b"
+    virtual_stages: int = 2
+    p2p: str = "auto"
     dp: int = 1
     # model
     model: str = "bert"
@@ -173,7 +175,12 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--debug-subset", action="store_true", default=False)
     # additions
     p.add_argument("--dp", type=int, default=1, help="pipeline replicas (PP x DP)")
-    p.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
+    p.add_argument("--schedule", choices=["1f1b", "gpipe", "interleaved"], default="1f1b",
+                   help="interleaved: interleaved 1F1B with --virtual-stages model chunks per rank")
+    p.add_argument("--virtual-stages", type=int, default=2,
+                   help="model chunks per rank under --schedule interleaved")
+    p.add_argument("--p2p", choices=["auto", "copy", "group"], default="auto",
+                   help="stage messages: copy-engine channels (one node) or NCCL/gloo groups")
     p.add_argument("--global-clip", action="store_true", default=False,
                    help="clip by the norm over all stages instead of per stage")
     p.add_argument("--ref-compat", action="store_true", default=False,
@@ -218,6 +225,8 @@ def build_global_config(args: argparse.Namespace) -> GlobalConfig:
         raise ValueError("hidden_size must be divisible by num_attention_heads")
     if args.dp < 1:
         raise ValueError("--dp must be >= 1")
+    if args.schedule == "interleaved" and args.virtual_stages < 1:
+        raise ValueError("--virtual-stages must be >= 1")
     dtype_name = args.autocast_dtype
     exp_id = make_exp_id(args.exp_mode, args.par_mode, args.reversible, args.is_pareprop, args.inverse,
                          args.checkpointing, dtype_name, args.dataset, args.seed, base["num_hidden_layers"])
@@ -225,7 +234,7 @@ def build_global_config(args: argparse.Namespace) -> GlobalConfig:
     return GlobalConfig(
         exp_mode=ExpMode(args.exp_mode), par_mode=ParMode(args.par_mode), is_pareprop=args.is_pareprop,
         reversible=args.reversible, inverse=args.inverse, checkpointing=args.checkpointing,
-        schedule=args.schedule, dp=args.dp,
+        schedule=args.schedule, virtual_stages=args.virtual_stages, p2p=args.p2p, dp=args.dp,
         autocast_dtype=DTYPES[dtype_name], dataset=args.dataset, debug_subset=args.debug_subset,
         batch_size=args.batch_size, microbatch_size=args.microbatch_size, num_microbatches=args.num_microbatches,
         num_epochs=args.num_epochs, lr=args.lr, gamma=args.gamma, global_clip=args.global_clip, seed=args.seed,

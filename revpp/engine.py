@@ -44,6 +44,19 @@ from revpp.utils.env import EnvContext
 from revpp.utils.profiling import annotate
 
 
+class ChunkedStage(torch.nn.Module):
+    """The model chunks of one rank under the interleaved schedule (state_dict keys
+    ``chunks.<c>.<stage keys>``)."""
+
+    def __init__(self, modules):
+        super().__init__()
+        self.chunks = torch.nn.ModuleList(modules)
+
+    @property
+    def kind(self) -> str:
+        return self.chunks[0].kind
+
+
 class DeviceWaitError(RuntimeError):
     """A kernel's bounded wait ran out of time (recorded in the device status word)."""
 
@@ -78,27 +91,53 @@ class Trainer:
         if self.local_batch % cfg.num_microbatches != 0:
             raise ValueError("local batch must be divisible by num_microbatches")
         self.mbs = self.local_batch // cfg.num_microbatches
-        # ---- model
-        self.module = build_stage_module(cfg, self.stage_index, self.P, stage_kind(cfg))
+        # ---- model: v chunks per rank (v > 1 with the interleaved schedule); chunk c is
+        # global stage c * P + stage_index of v * P
+        self.v = cfg.virtual_stages if cfg.schedule == "interleaved" else 1
+        if self.v > 1 and runtime_kind(cfg) == "inverse":
+            raise ValueError("the interleaved schedule supports reversible, standard and checkpoint stages")
+        G = self.P * self.v
+        modules = [build_stage_module(cfg, c * self.P + self.stage_index, G, stage_kind(cfg)) for c in range(self.v)]
+        self.module = modules[0] if self.v == 1 else ChunkedStage(modules)
         self.module.to(self.device)
         lowp = cfg.autocast_dtype == torch.bfloat16 and self.device.type == "cuda"
         self.flat = FlatParams(self.module, self.device, want_shadow=lowp)
         self.math = make_math(self.flat, cfg.autocast_dtype, cfg.num_attention_heads, self.device)
         self.uses_kernels = self.device.type == "cuda"
-        self.eh = make_embed_head(self.module, self.flat, cfg.autocast_dtype, self.device)
         kind = runtime_kind(cfg)
-        self.stage = STAGE_TYPES[kind](self.module, self.math, self.eh, self.mbs, cfg.num_microbatches, self.device,
-                                       pareprop=cfg.is_pareprop, eval_actv_err=eval_actv_err)
+        self.stages = []
+        for mm in modules:
+            eh = make_embed_head(mm, self.flat, cfg.autocast_dtype, self.device)
+            self.stages.append(STAGE_TYPES[kind](mm, self.math, eh, self.mbs, cfg.num_microbatches, self.device,
+                                                 pareprop=cfg.is_pareprop, eval_actv_err=eval_actv_err))
+        self.stage = self.stages[0]
+        self.eh = self.stage.eh
+        self.last_stage = self.stages[-1]
         # ---- communication (collective construction: every rank, same order)
         self.comms: Optional[PipeComms] = None
+        self.channels = None
         self.dp_group = None
         self.pp_group = None
+        self.p2p = "none"
         if dist.is_initialized():
-            label_spec = TensorSpec((self.local_batch,), torch.int64)
-            # messages into this stage: the previous stage's outputs, and the next stage's
-            # backward message for this receiver
-            self.comms = PipeComms(self.rank, world, self.P, self.D, self.device, self.stage.fwd_specs(),
-                                   self.stage.bwd_specs(self.stage_index), label_spec)
+            self.p2p = self._choose_p2p(cfg)
+            if self.v > 1 and self.p2p != "copy":
+                raise ValueError("the interleaved schedule runs over copy channels (--p2p copy, one node)")
+            if self.p2p == "group":
+                label_spec = TensorSpec((self.local_batch,), torch.int64)
+                # messages into this stage: the previous stage's outputs, and the next stage's
+                # backward message for this receiver
+                self.comms = PipeComms(self.rank, world, self.P, self.D, self.device, self.stage.fwd_specs(),
+                                       self.stage.bwd_specs(self.stage_index), label_spec)
+                if self.P > 1:
+                    self.pp_group = self.comms.group
+            else:
+                for d in range(self.D):
+                    g = dist.new_group(list(range(d * self.P, (d + 1) * self.P)))
+                    if d == self.replica:
+                        self.pp_group = g
+                if self.P > 1:
+                    self.channels = self._build_channels(cfg, kind)
             from revpp.parallel.p2p import _warm_group
 
             if self.D > 1:
@@ -108,14 +147,20 @@ class Trainer:
                     _warm_group(g, ranks, self.device)
                     if s == self.stage_index:
                         self.dp_group = g
-            if self.P > 1:
-                self.pp_group = self.comms.group
-        if self.P > 1 and self.device.type == "cuda":
+        if self.P > 1 and self.device.type == "cuda" and self.p2p == "group":
             from revpp import ops
 
             if ops.available():
                 ops.set_sm_reserve(4)  # room for the NCCL kernels that run next to the GEMMs
-        self.executor = PipelineExecutor(self.stage, self.comms, cfg.num_microbatches, cfg.schedule)
+        if self.channels is not None:
+            from revpp.parallel.schedule import ChannelExecutor
+
+            names = self._channel_names()
+            chans = {role: self.channels.get(name) for role, name in names.items()}
+            self.executor = ChannelExecutor(self.stages, chans, cfg.num_microbatches, self.P, self.stage_index,
+                                            cfg.schedule, global_rank=self.rank)
+        else:
+            self.executor = PipelineExecutor(self.stage, self.comms, cfg.num_microbatches, cfg.schedule)
         self.opt = FlatAdamW(self.flat, cfg.lr, eps=cfg.adam_eps, weight_decay=cfg.weight_decay,
                              max_grad_norm=cfg.max_grad_norm)
         self.lr_sched = StepLR(self.opt, 1, cfg.gamma)
@@ -131,6 +176,67 @@ class Trainer:
             self.dp_reducer = make_reducer(self, cfg)
         self.step_count = 0
 
+    # ------------------------------------------------------------------ p2p set-up
+    def _choose_p2p(self, cfg: GlobalConfig) -> str:
+        """"copy": copy-engine channels (every rank of the job on one node; shared memory on
+        CPU); "group": NCCL / gloo point-to-point groups.  ``auto`` picks copy channels on one
+        GPU node and groups otherwise (collective: every rank must agree)."""
+        import socket
+
+        want = cfg.p2p
+        hosts = [None] * dist.get_world_size()
+        dist.all_gather_object(hosts, socket.gethostname())
+        one_node = len(set(hosts)) == 1
+        if want == "auto":
+            want = "copy" if (one_node and self.device.type == "cuda") else "group"
+        if want == "copy" and not one_node:
+            raise ValueError("--p2p copy needs every rank on one node")
+        return want
+
+    def _channel_names(self) -> dict:
+        """This rank's channel roles -> channel names (see _build_channels)."""
+        P, r, d = self.P, self.stage_index, self.replica
+        names = {}
+        if r < P - 1 or self.v > 1:
+            names["fwd_out"] = f"d{d}:fwd:{r}"
+        if r > 0 or self.v > 1:
+            names["fwd_in"] = f"d{d}:fwd:{(r - 1) % P}"
+        if r > 0 or self.v > 1:
+            names["bwd_out"] = f"d{d}:bwd:{r}"
+        if r < P - 1 or self.v > 1:
+            names["bwd_in"] = f"d{d}:bwd:{(r + 1) % P}"
+        names["labels"] = f"d{d}:labels"
+        return names
+
+    def _build_channels(self, cfg: GlobalConfig, kind: str):
+        """Every pipeline channel of the job, in one order on every rank: per replica, the
+        forward channel out of each rank, the backward channel out of each rank, labels."""
+        from revpp.parallel.channels import ChannelSet, ChannelSpec
+        from revpp.parallel.schedule import min_channel_depth
+
+        P, v = self.P, self.v
+        act = TensorSpec((self.mbs, cfg.seq_len, cfg.hidden_size), torch.float32)
+        two_stream = kind in ("reversible", "inverse")
+        fwd = (act,) * (2 if two_stream else 1)
+        depth = min_channel_depth(P, v, cfg.num_microbatches, cfg.schedule) + 1
+        specs = []
+        for d in range(self.D):
+            base = d * P
+            for r in range(P):
+                if r < P - 1 or v > 1:
+                    specs.append(ChannelSpec(f"d{d}:fwd:{r}", base + r, base + (r + 1) % P, fwd, depth))
+            for r in range(P):
+                if r > 0 or v > 1:
+                    recv_stage = r - 1  # v == 1: the receiver is global stage r - 1
+                    if kind == "inverse" and recv_stage == 0:
+                        bwd = (act,) * 2
+                    else:
+                        bwd = (act,) * (4 if two_stream else 1)
+                    specs.append(ChannelSpec(f"d{d}:bwd:{r}", base + r, base + (r - 1) % P, bwd, depth))
+            specs.append(ChannelSpec(f"d{d}:labels", base, base + P - 1,
+                                     (TensorSpec((self.local_batch,), torch.int64),), 2))
+        return ChannelSet(specs, self.device)
+
     # ------------------------------------------------------------------ helpers
     @property
     def is_first(self) -> bool:
@@ -138,7 +244,11 @@ class Trainer:
 
     @property
     def is_last(self) -> bool:
-        return self.stage.is_last
+        return self.last_stage.is_last
+
+    @property
+    def actv_records(self) -> list:
+        return [r for st in self.stages for r in st.actv_records]
 
     def split_inputs(self, batch: dict):
         """Device micro-batch inputs of the first stage.  BERT passes the attention mask as
@@ -221,21 +331,24 @@ class Trainer:
         with torch.no_grad():
             losses = self.executor.step(inputs, labels, train=False)
         if self.is_last:
-            logits = torch.cat(self.stage.logits) if self.stage.logits else None
-            lab = torch.cat(self.stage.labels) if self.stage.labels is not None else None
+            st = self.last_stage
+            logits = torch.cat(st.logits) if st.logits else None
+            lab = torch.cat(st.labels) if st.labels is not None else None
             loss = torch.stack(losses).mean() if losses else None
             return loss, logits, lab
         return None
 
     def last_labels(self) -> Optional[torch.Tensor]:
-        return torch.cat(self.stage.labels) if self.stage.labels is not None else None
+        st = self.last_stage
+        return torch.cat(st.labels) if st.labels is not None else None
 
     def last_logits(self) -> Optional[torch.Tensor]:
-        return torch.cat(self.stage.logits) if self.stage.logits else None
+        st = self.last_stage
+        return torch.cat(st.logits) if st.logits else None
 
     def close(self) -> None:
-        if self.comms is not None:
-            self.comms.drain()
+        if self.channels is not None:
+            self.channels.close()
         if self.dp_reducer is not None and hasattr(self.dp_reducer, "close"):
             self.dp_reducer.close()
         self.check_device_status(sync=True)

@@ -219,5 +219,3 @@ class PipeComms:
             return [dist.P2POp(dist.irecv, buf, self.first_rank, self.group)], buf
         return [], None
 
-    def drain(self) -> None:
-        pass

@@ -11,7 +11,7 @@ Labels travel from the first to the last stage once per step, as in the referenc
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -281,3 +281,303 @@ class PipelineExecutor:
             bi += 1
         if cm is not None:
             cm.wait(send_h)
+
+
+# ============================================================================ virtual pipelines
+# A rank may hold several model chunks ("virtual stages").  Chunk c of rank r is global stage
+# g = c * P + r of G = v * P; its forward output goes to global stage g + 1 (rank r + 1, or
+# rank 0's next chunk when r = P - 1) and its backward message to g - 1.  Actions are
+# (kind, chunk, micro-batch).
+
+VAction = Tuple[str, int, int]
+
+
+def interleaved_1f1b(rank: int, num_stages: int, chunks: int, n: int) -> List[VAction]:
+    """Interleaved 1F1B (BERT/pipelining/schedules.py:1954, ScheduleInterleaved1F1B; the
+    Megatron-LM order): micro-batches go through the chunks in groups of P; the k-th forward
+    is chunk (k // P) % v of micro-batch (k // (P v)) P + k % P, the k-th backward the same
+    with the chunk order reversed.  Rank r runs 2 (P - r - 1) + (v - 1) P warm-up forwards,
+    then alternates one forward and one backward, then drains the backwards.  With v = 1
+    this is the ordinary 1F1B order."""
+    P, v = num_stages, chunks
+    if v == 1:
+        return [(k, 0, m) for k, m in one_f_one_b(rank, P, n)]
+    if n % P != 0:
+        raise ValueError(f"interleaved 1F1B needs the number of micro-batches ({n}) to be a multiple of "
+                         f"the pipeline depth ({P})")
+    total = n * v
+
+    def fwd(k):
+        return (k // P) % v, (k // (P * v)) * P + k % P
+
+    def bwd(k):
+        c, m = fwd(k)
+        return v - 1 - c, m
+
+    warm = total if n == P else min((P - rank - 1) * 2 + (v - 1) * P, total)
+    acts: List[VAction] = [("F",) + fwd(k) for k in range(warm)]
+    for k in range(total - warm):
+        acts.append(("F",) + fwd(warm + k))
+        acts.append(("B",) + bwd(k))
+    acts += [("B",) + bwd(k) for k in range(total - warm, total)]
+    return acts
+
+
+def virtual_actions(schedule: str, rank: int, num_stages: int, chunks: int, n: int, train: bool = True):
+    if not train:
+        if chunks == 1:
+            return [("F", 0, m) for m in range(n)]
+        return [a for a in interleaved_1f1b(rank, num_stages, chunks, n) if a[0] == "F"]
+    if schedule == "interleaved" or chunks > 1:
+        return interleaved_1f1b(rank, num_stages, chunks, n)
+    return [(k, 0, m) for k, m in SCHEDULES[schedule](rank, num_stages, n)]
+
+
+def _route(kind: str, rank: int, chunk: int, P: int):
+    """(peer rank, peer chunk) that the output of (kind, rank, chunk) goes to."""
+    if kind == "F":
+        return (rank + 1) % P, chunk + (1 if rank == P - 1 else 0)
+    return (rank - 1) % P, chunk - (1 if rank == 0 else 0)
+
+
+def simulate_virtual(num_stages: int, chunks: int, n: int, schedule: str = "interleaved", t_f: float = 1.0,
+                     t_b: float = 3.0, t_comm: float = 0.0, events: list | None = None):
+    """Timeline of a (virtual) pipeline schedule: every action of rank r starts when the rank
+    is free and its input has arrived (``t_comm`` after the producer finished; transfers run
+    beside compute).  ``t_f`` / ``t_b`` are per chunk.  Returns (makespan, per-rank busy).
+    Raises if the action orders deadlock."""
+    P, v = num_stages, chunks
+    G = P * v
+    acts = [virtual_actions(schedule, r, P, v, n) for r in range(P)]
+    pos = [0] * P
+    t = [0.0] * P
+    busy = [0.0] * P
+    fdone: Dict = {}
+    bdone: Dict = {}
+    progress = True
+    while progress:
+        progress = False
+        for r in range(P):
+            while pos[r] < len(acts[r]):
+                kind, c, m = acts[r][pos[r]]
+                g = c * P + r
+                if kind == "F":
+                    if g == 0:
+                        ready = 0.0
+                    else:
+                        src = fdone.get((g - 1, m))
+                        if src is None:
+                            break
+                        ready = src + t_comm
+                    dur = t_f
+                else:
+                    if g == G - 1:
+                        src = fdone.get((g, m))
+                        ready = src if src is not None else None
+                    else:
+                        src = bdone.get((g + 1, m))
+                        ready = None if src is None else src + t_comm
+                    if ready is None or (g, m) not in fdone:
+                        break
+                    dur = t_b
+                start = max(t[r], ready)
+                t[r] = start + dur
+                busy[r] += dur
+                (fdone if kind == "F" else bdone)[(g, m)] = t[r]
+                if events is not None:
+                    events.append((r, kind, c, m, start, t[r]))
+                pos[r] += 1
+                progress = True
+    if any(p < len(a) for p, a in zip(pos, acts)):
+        raise RuntimeError("schedule deadlocks")
+    return max(t), busy
+
+
+def host_deadlock_free(num_stages: int, chunks: int, n: int, schedule: str, depth: int, early_bwd_claim: bool = True,
+                       steps: int = 2) -> bool:
+    """Run the hosts of every rank of one pipeline through ``steps`` training steps with the
+    channel protocol (revpp.parallel.channels): an action waits for its input message to be
+    committed; the input is released after the action; sending message k on a channel waits
+    until the receiver released message k - depth.  With ``early_bwd_claim`` a backward claims
+    its output slot before releasing its input (the reconstructed stage input is sent before
+    the gradients are complete).  Returns False if some host would wait forever."""
+    P, v = num_stages, chunks
+    G = P * v
+    acts = [virtual_actions(schedule, r, P, v, n) for r in range(P)] if P > 1 else [[]]
+    # channel state: committed / released counts per (kind, src rank)
+    committed: Dict = {}
+    released: Dict = {}
+    # FIFO order check: the messages of a channel in sending order
+    sent_seq: Dict = {}
+    recv_seq: Dict = {}
+    for r in range(P):
+        for kind, c, m in acts[r]:
+            g = c * P + r
+            if kind == "F" and g < G - 1:
+                sent_seq.setdefault(("F", r), []).append(m * G + g + 1)
+            if kind == "B" and g > 0:
+                sent_seq.setdefault(("B", r), []).append(m * G + g - 1)
+            if kind == "F" and g > 0:
+                recv_seq.setdefault(("F", (r - 1) % P), []).append(m * G + g)
+            if kind == "B" and g < G - 1:
+                recv_seq.setdefault(("B", (r + 1) % P), []).append(m * G + g)
+    for key in sent_seq:
+        if sent_seq[key] != recv_seq.get(key):
+            raise RuntimeError(f"channel {key} is not consumed in sending order")
+    # per rank: (step, action index, phase) ; phase 0 = waiting input, 1 = waiting output slot
+    state = [[0, 0, 0] for _ in range(P)]
+    total = len(acts[0]) if P > 0 else 0
+    recv_count: Dict = {}
+    send_count: Dict = {}
+
+    def ch_in(kind, r):
+        return (kind, (r - 1) % P) if kind == "F" else (kind, (r + 1) % P)
+
+    progress = True
+    while progress:
+        progress = False
+        for r in range(P):
+            st = state[r]
+            while st[0] < steps:
+                if st[1] >= len(acts[r]):
+                    st[0], st[1], st[2] = st[0] + 1, 0, 0
+                    continue
+                kind, c, m = acts[r][st[1]]
+                g = c * P + r
+                needs_in = (kind == "F" and g > 0) or (kind == "B" and g < G - 1)
+                has_out = (kind == "F" and g < G - 1) or (kind == "B" and g > 0)
+                cin = ch_in(kind, r)
+                cout = (kind, r)
+                if st[2] == 0:
+                    if needs_in:
+                        k = recv_count.get(cin, 0)
+                        if committed.get(cin, 0) < k + 1:
+                            break
+                    st[2] = 1
+                    if not (early_bwd_claim and kind == "B") and needs_in:
+                        recv_count[cin] = recv_count.get(cin, 0) + 1
+                        released[cin] = recv_count[cin]
+                if st[2] == 1:
+                    if has_out:
+                        k = send_count.get(cout, 0)
+                        if released.get(cout, 0) < k - depth + 1:
+                            break
+                        send_count[cout] = k + 1
+                    if early_bwd_claim and kind == "B" and needs_in:
+                        recv_count[cin] = recv_count.get(cin, 0) + 1
+                        released[cin] = recv_count[cin]
+                    if has_out:
+                        committed[cout] = send_count[cout]
+                    st[1], st[2] = st[1] + 1, 0
+                    progress = True
+    del total
+    return all(s[0] >= steps for s in state)
+
+
+def min_channel_depth(num_stages: int, chunks: int, n: int, schedule: str, early_bwd_claim: bool = True,
+                      limit: int = 64) -> int:
+    """Smallest receive-ring depth with which the hosts cannot deadlock (at least 2)."""
+    for d in range(2, limit + 1):
+        if host_deadlock_free(num_stages, chunks, n, schedule, d, early_bwd_claim):
+            return d
+    raise RuntimeError("no ring depth up to %d avoids a deadlock for this schedule" % limit)
+
+
+class ChannelExecutor:
+    """Runs a (virtual) pipeline schedule on one rank over copy channels
+    (revpp.parallel.channels): every forward / backward sends its message as soon as it is
+    enqueued, and waits only for the message it consumes, so transfers overlap compute on
+    both GPUs.  A reversible backward sends the reconstructed stage input (X2, X1) as soon as
+    it exists and the gradients when they are done.
+
+    ``stages[c]`` is the runtime of chunk c; ``chans`` maps "fwd_in", "fwd_out", "bwd_in",
+    "bwd_out", "labels" to this rank's channels (absent where the rank has none)."""
+
+    def __init__(self, stages, chans: Dict[str, object], num_microbatches: int, num_stages: int, rank_in_pipe: int,
+                 schedule: str = "1f1b", early_x: bool = True, global_rank: int = 0):
+        self.stages = list(stages)
+        self.v = len(self.stages)
+        self.chans = chans
+        self.n = num_microbatches
+        self.P = num_stages
+        self.r = rank_in_pipe
+        self.schedule = schedule
+        self.early_x = early_x
+        self.global_rank = global_rank
+        self.train_actions = virtual_actions(schedule, self.r, self.P, self.v, self.n, train=True)
+        self.eval_actions = virtual_actions(schedule, self.r, self.P, self.v, self.n, train=False)
+        self.first = self.stages[0]
+        self.last = self.stages[-1]
+        # compatibility with the single-chunk executor
+        self.stage = self.first
+
+    def step(self, inputs: Optional[Sequence] = None, labels: Optional[torch.Tensor] = None, train: bool = True):
+        from .channels import ChannelError
+
+        for st in self.stages:
+            st.clear()
+        try:
+            lab_ch = self.chans.get("labels")
+            if lab_ch is not None:
+                if self.first.is_first:
+                    lab_ch.send([labels.to(self.first.device, non_blocking=True)])
+                if self.last.is_last:
+                    labels = lab_ch.recv()[0].clone()
+                    lab_ch.release()
+            if self.last.is_last:
+                self.last.labels = list(torch.tensor_split(labels, self.n)) if labels is not None else None
+            for kind, c, m in (self.train_actions if train else self.eval_actions):
+                if kind == "F":
+                    self._fwd(c, m, inputs, train)
+                else:
+                    self._bwd(c, m)
+        except ChannelError:
+            raise
+        except BaseException:
+            chs = [ch for ch in self.chans.values() if ch is not None]
+            if chs:
+                chs[0].counters.abort()  # the other ranks' next wait raises instead of timing out
+            raise
+        return self.last.losses
+
+    def _fwd(self, c, m, inputs, train):
+        from .faults import before_forward
+
+        st = self.stages[c]
+        if c == 0:
+            before_forward(self.global_rank, m)
+        cin = None
+        if st.is_first:
+            x = inputs[m]
+        else:
+            cin = self.chans["fwd_in"]
+            x = cin.recv()
+        out = st.forward(m, x, train)
+        if cin is not None:
+            cin.release()
+        if out is not None and not st.is_last:
+            self.chans["fwd_out"].send(out)
+
+    def _bwd(self, c, m):
+        st = self.stages[c]
+        msg = None
+        cin = None
+        if not st.is_last:
+            cin = self.chans["bwd_in"]
+            msg = cin.recv()
+        cout = None if st.is_first else self.chans["bwd_out"]
+        hook = None
+        if cout is not None and self.early_x and getattr(st, "kind", "") == "reversible":
+            def hook(x2, x1, _c=cout):
+                _c.put(2, x2)
+                _c.put(3, x1)
+        g = st.backward(m, msg, on_input=hook) if hook is not None else st.backward(m, msg)
+        if cin is not None:
+            cin.release()
+        if g is not None and cout is not None:
+            if hook is not None:
+                cout.put(0, g[0])
+                cout.put(1, g[1])
+                cout.commit()
+            else:
+                cout.send(g)

@@ -139,13 +139,20 @@ class ReversibleStage(StageBase):
             return None
         return (y2, y1)
 
-    def backward(self, mb, msg):
+    def backward(self, mb, msg, on_input=None):
+        """``on_input(x2, x1)``: called as soon as the stage input is reconstructed (before the
+        first block's gradients), so the executor can send the racts while they run."""
         if self.is_last:
             y2, y1, dy2, dy1 = self.last_cache.pop(mb)
         else:
             dy2, dy1, y2, y1 = msg
+        hook = None
+        if on_input is not None:
+            def hook(i, x2_, x1_):
+                if i == 0:
+                    on_input(x2_, x1_)
         (dx2, dx1), (x2, x1) = rev_backward(self.math, self.blocks, y2, y1, dy2, dy1, pareprop=self.pareprop,
-                                            streams=self.streams)
+                                            streams=self.streams, on_recover=hook)
         if self.eval_actv_err and mb in self.fwd_input_copy:
             self._record_actv_err(mb, (x2, x1), self.fwd_input_copy.pop(mb))
         if self.is_first:

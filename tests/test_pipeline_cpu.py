@@ -44,12 +44,16 @@ def _cfg(extra: str, world: int):
     return build_global_config(args)
 
 
-def _oracle(cfg, P, batch):
-    """Full network with ordinary autograd; returns (loss, {stage: {name: grad}})."""
-    mods = []
-    for s in range(P):
-        set_seed(cfg.seed + s)
-        mods.append(build_stage_module(cfg, s, P, stage_kind(cfg)))
+def _oracle(cfg, P, batch, v=1):
+    """Full network with ordinary autograd; returns (loss, {rank: {name: grad}}).  With
+    ``v`` chunks per rank, rank r builds global stages c * P + r (c = 0..v-1) in that order
+    after seeding, as the Trainer does, and its gradient names carry the chunk prefix."""
+    G = P * v
+    mods = [None] * G
+    for r in range(P):
+        set_seed(cfg.seed + r)
+        for c in range(v):
+            mods[c * P + r] = build_stage_module(cfg, c * P + r, G, stage_kind(cfg))
     flats = [FlatParams(m, "cpu", want_shadow=False) for m in mods]
     maths = [TorchMath(f, torch.float32, cfg.num_attention_heads) for f in flats]
     eh0 = TorchEmbedHead(mods[0], flats[0], torch.float32)
@@ -65,7 +69,7 @@ def _oracle(cfg, P, batch):
         x = eh0._embed(inputs[i])
         reversible = cfg.reversible
         x2, x1 = x, x
-        for s in range(P):
+        for s in range(G):
             for blk in mods[s].blocks:
                 if reversible:
                     y1 = x1 + maths[s].attn(blk.F, x2).float()
@@ -77,7 +81,12 @@ def _oracle(cfg, P, batch):
         logits = ehl._head(x2, x1 if reversible else None)
         total = total + Fn.cross_entropy(logits.float(), labels[i]) / n
     total.backward()
-    grads = [{name: p.grad.clone() for name, p in m.named_parameters() if p.grad is not None} for m in mods]
+    grads = [{} for _ in range(P)]
+    for g, m in enumerate(mods):
+        prefix = "" if v == 1 else f"chunks.{g // P}."
+        for name, p in m.named_parameters():
+            if p.grad is not None:
+                grads[g % P][prefix + name] = p.grad.clone()
     return float(total), grads
 
 
@@ -191,3 +200,35 @@ def test_pipeline_replicas_average_gradients():
             scale = r.abs().max().item()
             assert (g - r).abs().max().item() <= 1e-5 * max(scale, 1e-3), (s, name)
             assert torch.equal(g, g1[name]), (s, name)
+
+
+def _check(gathered, cfg, P, v=1):
+    batch = SyntheticBatches(cfg, cfg.batch_size, 1, seed=123).make(0)
+    ref_loss, ref_grads = _oracle(cfg, P, batch, v)
+    loss = gathered[P - 1][0]
+    assert abs(loss - ref_loss) <= 1e-5 * max(1.0, abs(ref_loss)), (loss, ref_loss)
+    for r in range(P):
+        got = gathered[r][1]
+        assert set(got) == set(ref_grads[r]), (sorted(got)[:5], sorted(ref_grads[r])[:5])
+        for name, g in got.items():
+            ref = ref_grads[r][name]
+            scale = ref.abs().max().item()
+            assert (g - ref).abs().max().item() <= 1e-5 * max(scale, 1e-3), f"rank {r} {name}"
+
+
+@pytest.mark.parametrize("extra,world", [
+    ("--reversible --p2p copy", 2),
+    ("--reversible --p2p copy --is_pareprop", 2),
+    ("--p2p copy --checkpointing", 2),
+    ("--reversible --p2p copy", 4),
+    ("--reversible --p2p copy --schedule interleaved --virtual-stages 2", 2),
+    ("--reversible --p2p copy --schedule interleaved --virtual-stages 2 --num-hidden-layers 8", 4),
+    ("--p2p copy --schedule interleaved --virtual-stages 2", 2),
+])
+def test_copy_channels_match_autograd(extra, world):
+    """Copy channels (shared-memory slots on CPU, the protocol of the GPU's copy-engine
+    channels) with 1F1B and interleaved 1F1B: same loss and gradients as autograd."""
+    gathered = _run(extra, world)
+    cfg = _cfg(extra, world)
+    v = cfg.virtual_stages if cfg.schedule == "interleaved" else 1
+    _check(gathered, cfg, world, v)
