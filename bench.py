@@ -66,6 +66,13 @@ def parse():
                    help="secondary workloads; the headline is bert-large")
     p.add_argument("--dp", type=int, default=1, help="pipeline replicas: PP = gpus / dp")
     p.add_argument("--stage", choices=["reversible", "standard", "checkpoint"], default="reversible")
+    p.add_argument("--schedule", choices=["1f1b", "interleaved"], default=None,
+                   help="default: interleaved 1F1B with several pipeline stages (revpp arm), 1f1b otherwise")
+    p.add_argument("--virtual-stages", type=int, default=None,
+                   help="model chunks per rank with the interleaved schedule (default: one block per chunk "
+                        "up to 3 chunks)")
+    p.add_argument("--p2p", choices=["auto", "copy", "group"], default="auto",
+                   help="stage messages: copy-engine channels or NCCL groups (revpp arm)")
     a = p.parse_args()
     if a.model != "bert-large" and a.layers == MODEL["layers"]:
         a.layers = None  # the preset's depth
@@ -73,7 +80,29 @@ def parse():
         p.error("--gpus must be a multiple of --dp")
     if a.microbatch_size is None:
         a.microbatch_size = 64 if a.gpus // a.dp == 1 else 16
+    P = a.gpus // a.dp
+    if a.schedule is None:
+        a.schedule = "interleaved" if (P > 1 and a.impl == "revpp" and a.p2p != "group") else "1f1b"
+    if a.virtual_stages is None:
+        a.virtual_stages = default_virtual_stages(a, P)
+    if a.schedule != "interleaved":
+        a.virtual_stages = 1
     return a
+
+
+def default_virtual_stages(a, P: int) -> int:
+    """Chunks per rank for the interleaved schedule: as many as keep at least one block per
+    chunk, at most 3, and a divisor of the blocks per rank."""
+    if P <= 1:
+        return 1
+    from revpp.config import PRESETS
+
+    layers = a.layers or PRESETS[a.model]["num_hidden_layers"]
+    per_rank = layers // P
+    for v in (3, 2):
+        if per_rank % v == 0:
+            return v
+    return 1
 
 
 MODEL_NAMES = {"bert-large": "Rev-BERT-Large", "bert-base": "Rev-BERT-Base", "vit-b16": "Rev-ViT-B/16",
@@ -141,7 +170,9 @@ def base_record(args, world, impl):
         "config": {"model": name, "layers": args.layers or pre["num_hidden_layers"], "hidden": pre["hidden_size"],
                    "heads": pre["num_attention_heads"], "global_batch": args.global_batch, "seq_len": seq,
                    "microbatch_size": args.microbatch_size, "num_microbatches": nmb,
-                   "parallelism": par, "schedule": "1f1b",
+                   "parallelism": par,
+                   "schedule": ("interleaved-1f1b" if args.schedule == "interleaved" else "1f1b"),
+                   "virtual_stages": args.virtual_stages,
                    "backward": "pareprop" if args.pareprop else "sequential",
                    "l2": "no flush: per-step working set (weights, Adam state, activations) >> 126 MB L2"},
     }
@@ -173,6 +204,7 @@ def run_revpp(args):
     par_mode = ParMode.PP if P > 1 or args.dp > 1 else ParMode.NONE
     cfg = GlobalConfig(par_mode=par_mode, reversible=args.stage == "reversible",
                        checkpointing=args.stage == "checkpoint", is_pareprop=args.pareprop, dp=args.dp,
+                       schedule=args.schedule, virtual_stages=args.virtual_stages, p2p=args.p2p,
                        autocast_dtype=torch.bfloat16, batch_size=args.global_batch,
                        microbatch_size=args.microbatch_size, num_microbatches=nmb, lr=1e-5, dataset="synthetic",
                        **pre)
@@ -237,6 +269,7 @@ def run_revpp(args):
     rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "e2e": e2e,
                 "gpu_launches": int(launches_total), "peak_hbm_gib": peak, "clocks": clocks,
                 "device_status": status})
+    rec["config"]["p2p"] = tr.p2p
     if loss_val is not None:
         rec["final_loss"] = loss_val
     # the loss lives on the last rank; rank 0 prints

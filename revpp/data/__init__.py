@@ -5,9 +5,11 @@ Vit/src/dataset_factory.py).
   attention mask, Bernoulli(0.5) labels; ViT pixels i.i.d. N(0, 1), labels uniform in
   [0, classes).  Batches are generated from (seed, batch index) so every run sees the
   same data, into pinned host memory.
-* ``imdb`` / ``debug`` (BERT) and ``cifar10`` / ``cifar100`` / ``cinic10`` / ``imagenet`` (ViT)
-  read pre-staged copies under ``--dataset-dir`` (no network).  The vocabulary size and
-  token-type count are fixed to bert-base-uncased's (30522, 2) instead of being fetched.
+* ``imdb`` / ``debug`` (BERT) read a raw or tokenised copy under ``--dataset-dir`` and
+  tokenise with a local BERT tokenizer directory; ``cifar10`` / ``cifar100`` / ``cinic10`` /
+  ``imagenet`` (ViT) read the reference's on-disk layouts through torchvision with the
+  reference's transforms (no network).  The vocabulary size and token-type count are fixed
+  to bert-base-uncased's (30522, 2) instead of being fetched.
 
 In pipeline mode only the first stage of each pipeline loads data, with local batch =
 global batch / replicas; the batch count is broadcast so every stage runs the same
@@ -112,14 +114,64 @@ class TensorBatches:
 
 
 # ------------------------------------------------------------------ pre-staged real datasets
+def _tokenize(texts: List[str], labels: List[int], tokenizer_dir: Path, max_length: int) -> Dict[str, torch.Tensor]:
+    """BERT word-piece tokenisation with the reference's settings (special tokens, padding
+    and truncation to max_length; BERT/src/dataset_factory.py:44-67), from a local tokenizer
+    directory (no download)."""
+    from transformers import BertTokenizerFast
+
+    tok = BertTokenizerFast.from_pretrained(str(tokenizer_dir))
+    enc = tok(texts, add_special_tokens=True, max_length=max_length, padding="max_length", truncation=True,
+              return_tensors="pt")
+    return {"input_ids": enc["input_ids"].to(torch.int64), "attention_mask": enc["attention_mask"].to(torch.int64),
+            "labels": torch.tensor(labels, dtype=torch.int64)}
+
+
+def _imdb_texts(root: Path, split: str):
+    """(texts, labels) of an IMDb split from a raw copy: the HF ``save_to_disk`` layout the
+    reference's prepare script writes (imdb_raw/), or the original aclImdb text folders."""
+    raw = root / "imdb_raw"
+    if raw.exists():
+        from datasets import load_from_disk
+
+        d = load_from_disk(str(raw))[split]
+        return list(d["text"]), [int(x) for x in d["label"]]
+    acl = root / "aclImdb" / split
+    if acl.exists():
+        texts, labels = [], []
+        for lab, sub in ((0, "neg"), (1, "pos")):
+            for f in sorted((acl / sub).glob("*.txt")):
+                texts.append(f.read_text(encoding="utf-8", errors="replace"))
+                labels.append(lab)
+        return texts, labels
+    return None
+
+
 def _load_imdb(cfg: GlobalConfig, split: str) -> Dict[str, torch.Tensor]:
-    root = cfg.dataset_rdir / "imdb_tokenized"
-    f = root / f"{split}.pt"
-    if not f.exists():
+    """IMDb, in this order: a tokenised tensor cache (imdb_tokenized/{split}.pt), else the raw
+    text (imdb_raw/ or aclImdb/) tokenised with the local tokenizer/ directory (written to the
+    cache when the directory is writable)."""
+    root = cfg.dataset_rdir
+    S = cfg.max_position_embeddings
+    cache = root / "imdb_tokenized" / f"{split}.pt"
+    if cache.exists():
+        d = torch.load(cache)
+        if d["input_ids"].shape[1] == S:
+            return d
+    raw = _imdb_texts(root, split)
+    tok_dir = root / "tokenizer"
+    if raw is None or not tok_dir.exists():
         raise FileNotFoundError(
-            f"IMDb needs a pre-tokenized copy at {f} (dict of input_ids / attention_mask / labels tensors); "
-            "there is no network access to download it.  Use --dataset synthetic for benchmarks.")
-    return torch.load(f)
+            f"IMDb needs {cache}, or a raw copy ({root / 'imdb_raw'} or {root / 'aclImdb'}) and a BERT tokenizer "
+            f"directory {tok_dir}; there is no network access (python -m revpp.data.prepare stages them). "
+            "Use --dataset synthetic for benchmarks.")
+    d = _tokenize(raw[0], raw[1], tok_dir, S)
+    try:
+        cache.parent.mkdir(parents=True, exist_ok=True)
+        torch.save(d, cache)
+    except OSError:
+        pass
+    return d
 
 
 _DEBUG_SENTENCES = [
@@ -130,27 +182,31 @@ _DEBUG_SENTENCES = [
 
 
 def _load_debug(cfg: GlobalConfig, split: str) -> Dict[str, torch.Tensor]:
-    """Tiny sentiment set tokenised with a hash vocabulary (no tokenizer download)."""
+    """Tiny sentiment set (30 sentences, the same for train and validation as in the
+    reference's debug set); tokenised with the local tokenizer directory when there is one,
+    else with a hash vocabulary."""
     S = cfg.max_position_embeddings
-    ids, labels = [], []
-    for i, s in enumerate(_DEBUG_SENTENCES * 3):
+    sents = _DEBUG_SENTENCES * 3
+    labels = [i % 2 for i in range(len(sents))]
+    tok_dir = cfg.dataset_rdir / "tokenizer"
+    if tok_dir.exists():
+        return _tokenize(sents, labels, tok_dir, S)
+    ids = []
+    for s in sents:
         toks = [101] + [1000 + (hash(w) % (cfg.vocab_size - 1000)) for w in s.split()][: S - 2] + [102]
-        toks = toks + [0] * (S - len(toks))
-        ids.append(toks)
-        labels.append(i % 2)
+        ids.append(toks + [0] * (S - len(toks)))
     ids_t = torch.tensor(ids, dtype=torch.int64)
     return {"input_ids": ids_t, "attention_mask": (ids_t != 0).to(torch.int64),
             "labels": torch.tensor(labels, dtype=torch.int64)}
 
 
-def _load_cifar(cfg: GlobalConfig, split: str, name: str) -> Dict[str, torch.Tensor]:
+def _load_cifar_pickle(cfg: GlobalConfig, split: str, name: str) -> Dict[str, torch.Tensor]:
+    """CIFAR from the python-pickle release unpacked directly under the dataset directory."""
     import pickle
 
     import numpy as np
 
     root = cfg.dataset_rdir / {"cifar10": "cifar-10-batches-py", "cifar100": "cifar-100-python"}[name]
-    if not root.exists():
-        raise FileNotFoundError(f"{name} needs the python-pickle release under {root} (no network access)")
     files = ([f"data_batch_{i}" for i in range(1, 6)] if split == "train" else ["test_batch"]) \
         if name == "cifar10" else (["train"] if split == "train" else ["test"])
     xs, ys = [], []
@@ -160,9 +216,8 @@ def _load_cifar(cfg: GlobalConfig, split: str, name: str) -> Dict[str, torch.Ten
         xs.append(np.asarray(d["data"], dtype=np.uint8).reshape(-1, 3, 32, 32))
         ys.extend(d["labels"] if "labels" in d else d["fine_labels"])
     x = torch.from_numpy(np.concatenate(xs)).float().div_(255.0)
-    mean = torch.tensor([0.4914, 0.4822, 0.4465]).view(1, 3, 1, 1)
-    std = torch.tensor([0.2470, 0.2435, 0.2616]).view(1, 3, 1, 1)
-    x = (x - mean) / std
+    mean, std = _NORM[name]
+    x = (x - torch.tensor(mean).view(1, 3, 1, 1)) / torch.tensor(std).view(1, 3, 1, 1)
     if cfg.img_size != 32 and name == "cifar10":
         # the reference resizes CIFAR-10 to 224 (Vit/src/dataset_factory.py:31-57)
         x = torch.nn.functional.interpolate(x, size=(cfg.img_size, cfg.img_size), mode="bilinear",
@@ -170,14 +225,97 @@ def _load_cifar(cfg: GlobalConfig, split: str, name: str) -> Dict[str, torch.Ten
     return {"images": x, "labels": torch.tensor(ys, dtype=torch.int64)}
 
 
+# normalisation constants of the reference's transforms (Vit/src/dataset_factory.py)
+_NORM = {
+    "cifar10": ([0.4914, 0.4822, 0.4465], [0.2023, 0.1994, 0.2010]),
+    "cinic10": ([0.4914, 0.4822, 0.4465], [0.2023, 0.1994, 0.2010]),
+    "cifar100": ([0.5071, 0.4865, 0.4409], [0.2673, 0.2564, 0.2761]),
+    "imagenet": ([0.485, 0.456, 0.406], [0.229, 0.224, 0.225]),
+}
+
+
+def image_dataset(cfg: GlobalConfig, split: str):
+    """A torchvision dataset of (image, label) with the reference's transforms
+    (Vit/src/dataset_factory.py:5-109), read from its on-disk layout under --dataset-dir:
+
+      cifar10   cifar-10/  (torchvision CIFAR10 files)   224 x 224: resize, crop pad 4, flip
+      cifar100  cifar-100/ (torchvision CIFAR100 files)  32 x 32: crop pad 4, flip
+      cinic10   CINIC-10/{train,valid}/<class>/*.png     32 x 32: crop pad 4, flip
+      imagenet  ImageNet-1K/{train,val}/<class>/*.JPEG   train: random-resized crop 224 (scale
+                0.2-1, bicubic), flip; val: resize 256, centre crop 224
+    Returns None when the layout is absent."""
+    from torchvision import datasets as tvd
+    from torchvision import transforms as T
+
+    name, root, train = cfg.dataset, cfg.dataset_rdir, split == "train"
+    norm = T.Normalize(*_NORM[name])
+    if name == "cifar10":
+        size = cfg.img_size
+        tf = T.Compose(([T.Resize((size, size)), T.RandomCrop(size, padding=4), T.RandomHorizontalFlip()] if train
+                        else [T.Resize((size, size))]) + [T.ToTensor(), norm])
+        d = root / "cifar-10"
+        if not (d / "cifar-10-batches-py").exists():
+            return None
+        return tvd.CIFAR10(str(d), train=train, transform=tf, download=False)
+    if name == "cifar100":
+        tf = T.Compose(([T.RandomCrop(32, padding=4), T.RandomHorizontalFlip()] if train else []) + [T.ToTensor(), norm])
+        d = root / "cifar-100"
+        if not (d / "cifar-100-python").exists():
+            return None
+        return tvd.CIFAR100(str(d), train=train, transform=tf, download=False)
+    if name == "cinic10":
+        tf = T.Compose(([T.RandomCrop(32, padding=4), T.RandomHorizontalFlip()] if train else []) + [T.ToTensor(), norm])
+        d = root / "CINIC-10" / ("train" if train else "valid")
+        return tvd.ImageFolder(str(d), tf) if d.exists() else None
+    if name == "imagenet":
+        size = cfg.img_size
+        if train:
+            tf = T.Compose([T.RandomResizedCrop(size, scale=(0.2, 1.0), interpolation=T.InterpolationMode.BICUBIC),
+                            T.RandomHorizontalFlip(), T.ToTensor(), norm])
+        else:
+            tf = T.Compose([T.Resize(int(size * 256 / 224)), T.CenterCrop(size), T.ToTensor(), norm])
+        d = root / "ImageNet-1K" / ("train" if train else "val")
+        return tvd.ImageFolder(str(d), tf) if d.exists() else None
+    return None
+
+
+class ImageBatches:
+    """Batches {"images", "labels"} from a torchvision dataset through a DataLoader with
+    workers; replicas read disjoint shards (DistributedSampler over the replicas)."""
+
+    def __init__(self, ds, batch_size: int, train: bool, replicas: int, replica: int, seed: int, workers: int):
+        from torch.utils.data import DataLoader, DistributedSampler
+
+        self.sampler = DistributedSampler(ds, num_replicas=replicas, rank=replica, shuffle=train, seed=seed,
+                                          drop_last=True)
+        self.loader = DataLoader(ds, batch_size=batch_size, sampler=self.sampler, num_workers=workers,
+                                 pin_memory=torch.cuda.is_available(), drop_last=True,
+                                 persistent_workers=workers > 0)
+
+    def __len__(self) -> int:
+        return len(self.loader)
+
+    def set_epoch(self, e: int) -> None:
+        self.sampler.set_epoch(e)
+
+    def __iter__(self):
+        for x, y in self.loader:
+            yield {"images": x, "labels": y}
+
+
 def load_split(cfg: GlobalConfig, split: str) -> Dict[str, torch.Tensor]:
+    """In-memory tensors of a split (text datasets and CIFAR from the pickle release)."""
     if cfg.dataset == "imdb":
         return _load_imdb(cfg, split)
     if cfg.dataset == "debug":
         return _load_debug(cfg, split)
     if cfg.dataset in ("cifar10", "cifar100"):
-        return _load_cifar(cfg, split, cfg.dataset)
-    raise FileNotFoundError(f"dataset {cfg.dataset} has no offline copy in {cfg.dataset_rdir}")
+        pick = cfg.dataset_rdir / {"cifar10": "cifar-10-batches-py", "cifar100": "cifar-100-python"}[cfg.dataset]
+        if pick.exists():
+            return _load_cifar_pickle(cfg, split, cfg.dataset)
+    raise FileNotFoundError(
+        f"dataset {cfg.dataset} has no offline copy under {cfg.dataset_rdir} (see revpp.data.image_dataset for "
+        "the layouts; python -m revpp.data.prepare stages them)")
 
 
 @dataclass
@@ -204,13 +342,25 @@ def build_loaders(cfg: GlobalConfig, rank: int, world: int, num_stages: int, dev
             train = SyntheticBatches(cfg, local_batch, nb, seed, "train")
             val = SyntheticBatches(cfg, local_batch, max(1, nb // 4), seed, "val")
         else:
-            tr = load_split(cfg, "train")
-            va = load_split(cfg, "test")
-            if cfg.debug_subset:
-                tr = {k: v[: 8 * local_batch] for k, v in tr.items()}
-                va = {k: v[: 2 * local_batch] for k, v in va.items()}
-            train = TensorBatches(tr, local_batch, True, seed)
-            val = TensorBatches(va, local_batch, False, seed)
+            replica = rank // max(1, num_stages) if cfg.par_mode == ParMode.PP else rank
+            ds_tr = image_dataset(cfg, "train") if REGISTRY[cfg.dataset].kind == "image" else None
+            if ds_tr is not None:
+                ds_va = image_dataset(cfg, "val")
+                if cfg.debug_subset:
+                    from torch.utils.data import Subset
+
+                    ds_tr = Subset(ds_tr, range(min(len(ds_tr), 8 * local_batch * replicas)))
+                    ds_va = Subset(ds_va, range(min(len(ds_va), 2 * local_batch * replicas)))
+                train = ImageBatches(ds_tr, local_batch, True, replicas, replica, cfg.seed, cfg.num_workers)
+                val = ImageBatches(ds_va, local_batch, False, replicas, replica, cfg.seed, cfg.num_workers)
+            else:
+                tr = load_split(cfg, "train")
+                va = load_split(cfg, "test")
+                if cfg.debug_subset:
+                    tr = {k: v[: 8 * local_batch] for k, v in tr.items()}
+                    va = {k: v[: 2 * local_batch] for k, v in va.items()}
+                train = TensorBatches(tr, local_batch, True, seed)
+                val = TensorBatches(va, local_batch, False, seed)
         nt, nv = len(train), len(val)
     if dist.is_initialized() and cfg.par_mode == ParMode.PP:
         t = torch.tensor([nt, nv], dtype=torch.int64, device=device)
