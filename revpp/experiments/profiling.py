@@ -9,7 +9,10 @@ events.  Outputs under ``profiles/{exp_id}/{mbs}x{nmb}/{env_id}/rank{r}/``:
   memory.json                memory timeline (torch.profiler export), when available
   performance_stats.json     step times (device, max over ranks), throughput
                              (global batch * active steps / active duration), span stats
-  timeline_peak_stats.json   peak allocated / reserved memory and the predicted peak
+  timeline_peak_stats.json   peak allocated / reserved memory, the peak's breakdown by
+                             category (torch's memory-timeline categories, as the reference
+                             reports them, and this framework's own buffer accounting),
+                             and the predicted peak
 """
 from __future__ import annotations
 
@@ -24,6 +27,7 @@ from revpp.utils.profiling import DeviceTimer, max_over_ranks
 from .base import Experiment
 from .events import parse_event_spans, span_stats
 from .memory_predictor import predict_peak_bytes
+from .memory_report import framework_breakdown, profiler_peak_breakdown
 
 
 class ProfilingExperiment(Experiment):
@@ -88,8 +92,13 @@ class ProfilingExperiment(Experiment):
         (out / "performance_stats.json").write_text(json.dumps(stats, indent=2))
         peak = {}
         if env.device.type == "cuda":
-            peak = {"cuda_max_alloc_gib": torch.cuda.max_memory_allocated() / 2**30,
-                    "cuda_max_reserved_gib": torch.cuda.max_memory_reserved() / 2**30}
+            alloc = torch.cuda.max_memory_allocated()
+            peak = {"cuda_max_alloc_gib": alloc / 2**30,
+                    "cuda_max_reserved_gib": torch.cuda.max_memory_reserved() / 2**30,
+                    "framework_peak_breakdown_gib": framework_breakdown(t, alloc)}
+            prof_peak = profiler_peak_breakdown(out / "memory.json")
+            if prof_peak is not None:
+                peak.update(prof_peak)
         peak["predicted_peak_gib"] = predict_peak_bytes(cfg, t.stage_index, t.P, t.stage.kind,
                                                         pareprop=cfg.is_pareprop) / 2**30
         (out / "timeline_peak_stats.json").write_text(json.dumps(peak, indent=2))

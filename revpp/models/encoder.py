@@ -12,7 +12,8 @@ Submodule names follow the reference so ``state_dict`` keys match:
 
   kind        first stage          middle / last stage     single-stage (PP=1)
   reversible  rev.layers.{i}.F/G   mod.layers.{i}.F/G      body.layers.{i}.F/G
-  standard    rev.{i}.F/G          mod.{i}.F/G             rev.{i}.F/G
+  standard    rev.{i}.F/G (BERT)   mod.{i}.F/G             body.{i}.F/G
+              body.{i}.F/G (ViT)
   inverse     rev.{i}.F/G          mod.{i}.F/G             body.{i}.F/G
 
 Pooling: reversible BERT averages over the sequence (bert_stages.py:440); standard BERT,
@@ -65,7 +66,14 @@ class EncoderStage(nn.Module):
             setattr(self, name, _Layers(blocks))
             self._body_prefix = f"{name}.layers"
         else:
-            name = ("body" if (single and kind == "inverse") else "rev") if self.is_first else "mod"
+            # reference container names: full stages "body"; first stages "rev", except the
+            # standard ViT first stage ("body", Vit/models/normal_vit_stages.py:105); others "mod"
+            if single:
+                name = "body"
+            elif self.is_first:
+                name = "body" if (kind == "standard" and cfg.model == "vit") else "rev"
+            else:
+                name = "mod"
             setattr(self, name, nn.ModuleList(blocks))
             self._body_prefix = name
         self.blocks: List[EncoderBlock] = blocks

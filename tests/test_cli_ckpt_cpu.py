@@ -164,3 +164,24 @@ def test_bench_paber_microbatch_default(monkeypatch):
         a = bench.parse()
         assert a.microbatch_size == want, (argv, a.microbatch_size)
         assert a.global_batch % (a.microbatch_size * a.dp) == 0
+
+
+def test_profiler_peak_breakdown_from_memory_timeline(tmp_path):
+    """The peak of a memory timeline export and its split by category, as the reference's
+    timeline_peak_stats.json reports it."""
+    import json
+
+    from revpp.experiments.memory_report import BASE_CATS, profiler_peak_breakdown
+
+    G = 1 << 30
+    rows = [[0] * len(BASE_CATS) for _ in range(3)]
+    rows[1][BASE_CATS.index("PARAMETER")] = 2 * G
+    rows[1][BASE_CATS.index("ACTIVATION")] = 3 * G
+    rows[2][BASE_CATS.index("PARAMETER")] = 2 * G
+    rows[2][BASE_CATS.index("CATEGORY_0")] = 9 * G  # not a plotted category
+    path = tmp_path / "memory.json"
+    path.write_text(json.dumps([[1000, 2000, 3000], rows]))
+    r = profiler_peak_breakdown(path)
+    assert r["peak_total_gib"] == 5.0 and r["timestamp_ms"] == 1.0
+    assert r["profiler_peak_breakdown_gib"] == {"PARAMETER": 2.0, "ACTIVATION": 3.0}
+    assert profiler_peak_breakdown(tmp_path / "missing.json") is None
