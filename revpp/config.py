@@ -31,6 +31,8 @@ class ParMode(enum.Enum):
     PP = "pp"
 
 
+DATASET_ALIASES = {"cifar-10": "cifar10", "cifar-100": "cifar100"}
+
 DTYPES = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
 DTYPE_NAMES = {v: k for k, v in DTYPES.items()}
 
@@ -152,7 +154,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--is_pareprop", "--is-pareprop", dest="is_pareprop", action="store_true", default=False)
     p.add_argument("--checkpointing", action="store_true", default=False)
     p.add_argument("--dataset", default="synthetic",
-                   choices=["synthetic", "imdb", "debug", "cifar10", "cifar100", "cinic10", "imagenet"])
+                   choices=["synthetic", "imdb", "debug", "cifar10", "cifar100", "cinic10", "imagenet",
+                            "cifar-10", "cifar-100"],
+                   help="cifar-10 / cifar-100 are the reference's spellings of cifar10 / cifar100")
     p.add_argument("--model", choices=["bert", "vit"], default=None)
     p.add_argument("--preset", choices=sorted(PRESETS), default=None)
     p.add_argument("--num-hidden-layers", type=int, default=None)
@@ -235,7 +239,8 @@ def build_global_config(args: argparse.Namespace) -> GlobalConfig:
         exp_mode=ExpMode(args.exp_mode), par_mode=ParMode(args.par_mode), is_pareprop=args.is_pareprop,
         reversible=args.reversible, inverse=args.inverse, checkpointing=args.checkpointing,
         schedule=args.schedule, virtual_stages=args.virtual_stages, p2p=args.p2p, dp=args.dp,
-        autocast_dtype=DTYPES[dtype_name], dataset=args.dataset, debug_subset=args.debug_subset,
+        autocast_dtype=DTYPES[dtype_name], dataset=DATASET_ALIASES.get(args.dataset, args.dataset),
+        debug_subset=args.debug_subset,
         batch_size=args.batch_size, microbatch_size=args.microbatch_size, num_microbatches=args.num_microbatches,
         num_epochs=args.num_epochs, lr=args.lr, gamma=args.gamma, global_clip=args.global_clip, seed=args.seed,
         synthetic_batches=args.synthetic_batches,

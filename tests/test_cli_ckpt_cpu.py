@@ -185,3 +185,21 @@ def test_profiler_peak_breakdown_from_memory_timeline(tmp_path):
     assert r["peak_total_gib"] == 5.0 and r["timestamp_ms"] == 1.0
     assert r["profiler_peak_breakdown_gib"] == {"PARAMETER": 2.0, "ACTIVATION": 3.0}
     assert profiler_peak_breakdown(tmp_path / "missing.json") is None
+
+
+@pytest.mark.parametrize("script", ["bert_actv_err.sh", "vit_profiling.sh"])
+def test_launch_scripts_run_small(tmp_path, script):
+    """The launch scripts of the reference's run configurations start the CLI with its
+    flags; later flags (EXTRA) shrink the model so the run fits a CPU test."""
+    extra = (f"--device cpu --synthetic-batches 1 --num-hidden-layers 4 --hidden-size 64 --num-attention-heads 2 "
+             f"--batch-size 8 --microbatch-size 2 --num-microbatches 4 --log-dir {tmp_path}/logs "
+             f"--profile-dir {tmp_path}/prof --checkpoint-dir {tmp_path}/ckpt")
+    if script.startswith("bert"):
+        extra += " --max-position-embeddings 32"
+    else:
+        extra += " --img-size 32 --patch-size 16"
+    env = dict(os.environ, NPROC="2", DATASET="synthetic", DTYPE="fp32", EXTRA=extra, MASTER_PORT=str(_port()),
+               OMP_NUM_THREADS="1")
+    p = subprocess.run(["bash", os.path.join(ROOT, "launch", script)], capture_output=True, text=True, timeout=600,
+                       cwd=ROOT, env=env)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
