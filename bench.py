@@ -285,74 +285,130 @@ def run_revpp(args):
 
 
 # ============================================================================ reference arm
-REF_ROOT = os.path.join(HERE, "baseline", "_ref", "BERT")
+REF_BASE = os.path.join(HERE, "baseline", "_ref")
+
+
+def _ref_modules(args, world, rank, dev):
+    """The reference's own stage module for this rank and its pipeline-stage class
+    (BERT/experiment/base.py:165-278; Vit/experiment/base.py): reversible stages run in
+    RevPipelineStageWithPareprop, standard ones in PipelineStage, activation-checkpoint
+    ones in PipelineStageWithCP."""
+    from revpp.config import PRESETS
+
+    pre = PRESETS[args.model]
+    bert = pre["model"] == "bert"
+    sys.path.insert(0, os.path.join(REF_BASE, "BERT" if bert else "Vit"))
+    import pipelining as refpp  # noqa: E402
+
+    layers = args.layers or pre["num_hidden_layers"]
+    kw = dict(hidden_size=pre["hidden_size"], num_attention_heads=pre["num_attention_heads"],
+              num_blocks=layers // world, enable_amp=True, autocast_dtype=torch.bfloat16)
+    rev = args.stage == "reversible"
+    if rev:
+        kw["is_pareprop"] = args.pareprop
+    first, last = rank == 0, rank == world - 1
+    if bert:
+        if rev:
+            from models.bert_stages import BertFirstStage as F, BertLastStage as L, BertMidStage as Mid  # noqa: E402
+        else:
+            from models.normal_bert_stages import (NormalBertFirstStage as F, NormalBertLastStage as L,  # noqa: E402
+                                                   NormalBertMidStage as Mid)
+        if first:
+            model = F(vocab_size=MODEL["vocab"], max_position_embeddings=args.seq, type_vocab_size=2, **kw)
+        elif last:
+            model = L(num_classes=pre["num_classes"], **kw)
+        else:
+            model = Mid(**kw)
+    else:
+        if rev:
+            from models.vit_stages import ViTFirstStage as F, ViTLastStage as L, ViTMidStage as Mid  # noqa: E402
+        else:
+            from models.normal_vit_stages import (NormalViTFirstStage as F, NormalViTLastStage as L,  # noqa: E402
+                                                  NormalViTMidStage as Mid)
+        img = dict(img_size=pre["img_size"], patch_size=pre["patch_size"], in_chans=3)
+        if first:
+            model = F(**img, **kw)
+        elif last:
+            model = L(num_classes=pre["num_classes"], **kw)
+        else:
+            model = Mid(**kw)
+    stage_cls = {"reversible": refpp.RevPipelineStageWithPareprop, "standard": refpp.PipelineStage,
+                 "checkpoint": refpp.PipelineStageWithCP}[args.stage]
+    return model.to(dev), stage_cls, refpp.Schedule1F1B, pre
 
 
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if args.model != "bert-large" or args.dp != 1 or args.stage != "reversible":
+    if args.dp != 1:
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "the reference arm runs the headline workload "
-                              "(reversible BERT-Large, pure PP) only"}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no pipeline replicas (PP x DP): "
+                              "its DDP/FSDP modes and its PP mode share the world group "
+                              "(BERT/experiment/base.py:244-299)"}), flush=True)
         return
-    if not os.path.isdir(REF_ROOT):
+    if not os.path.isdir(REF_BASE):
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
         return
     if world < 2:
+        if args.stage == "reversible":
+            why = ("the reference cannot train a reversible model on one GPU: PP=1 builds a first stage without a "
+                   "head (BERT/experiment/base.py:166) and its non-PP reversible model computes no body gradients "
+                   "(BERT/models/reversible.py:125)")
+        elif args.model.startswith("bert"):
+            why = ("the reference's single-GPU BERT path fails: its engine passes attention_mask to a stage forward "
+                   "that does not take it (BERT/src/engine.py:137 vs BERT/models/bert_stages.py:111)")
+        else:
+            why = "this arm measures the reference's pipeline path (Schedule1F1B), which needs at least 2 GPUs"
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference cannot train reversible BERT on one GPU: PP=1 builds a first stage "
-                              "without a head (BERT/experiment/base.py:166) and its non-PP reversible model "
-                              "computes no body gradients (BERT/models/reversible.py:125)"}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
     world, rank, local, dev = dist_setup(args.gpus)
-    sys.path.insert(0, REF_ROOT)
-    from models.bert_stages import BertFirstStage, BertLastStage, BertMidStage  # noqa: E402
-    from pipelining import RevPipelineStageWithPareprop, Schedule1F1B  # noqa: E402
-
     from revpp.utils.clocks import ClockSampler  # timing helper only
 
     torch.manual_seed(rank)
     nmb = args.global_batch // args.microbatch_size
-    kw = dict(hidden_size=MODEL["hidden"], num_attention_heads=MODEL["heads"], num_blocks=args.layers // world,
-              enable_amp=True, autocast_dtype=torch.bfloat16, is_pareprop=args.pareprop)
-    if rank == 0:
-        model = BertFirstStage(vocab_size=MODEL["vocab"], max_position_embeddings=args.seq, type_vocab_size=2, **kw)
-    elif rank == world - 1:
-        model = BertLastStage(num_classes=MODEL["classes"], **kw)
-    else:
-        model = BertMidStage(**kw)
-    model = model.to(dev)
-    stage = RevPipelineStageWithPareprop(submodule=model, stage_index=rank, num_stages=world, device=dev)
-    sched = Schedule1F1B(stage=stage, n_microbatches=nmb, loss_fn=torch.nn.CrossEntropyLoss())
+    model, stage_cls, sched_cls, pre = _ref_modules(args, world, rank, dev)
+    bert = pre["model"] == "bert"
+    stage = stage_cls(submodule=model, stage_index=rank, num_stages=world, device=dev)
+    sched = sched_cls(stage=stage, n_microbatches=nmb, loss_fn=torch.nn.CrossEntropyLoss())
     opt = torch.optim.AdamW(model.parameters(), lr=1e-5, weight_decay=0.01, eps=1e-6)
     g = torch.Generator().manual_seed(0)
     B, S = args.global_batch, args.seq
-    host = [dict(ids=torch.randint(0, MODEL["vocab"], (B, S), generator=g).pin_memory(),
-                 mask=torch.ones(B, S, dtype=torch.int64).pin_memory(),
-                 labels=torch.bernoulli(torch.full((B,), 0.5), generator=g).long().pin_memory()) for _ in range(2)]
+    if bert:
+        host = [dict(ids=torch.randint(0, MODEL["vocab"], (B, S), generator=g).pin_memory(),
+                     mask=torch.ones(B, S, dtype=torch.int64).pin_memory(),
+                     labels=torch.bernoulli(torch.full((B,), 0.5), generator=g).long().pin_memory()) for _ in range(2)]
+    else:
+        I = pre["img_size"]
+        host = [dict(images=torch.randn(B, 3, I, I, generator=g).pin_memory(),
+                     labels=torch.randint(0, pre["num_classes"], (B,), generator=g).pin_memory()) for _ in range(2)]
     labels_buf = torch.zeros(B, dtype=torch.int64, device=dev)
 
     def step(i):
-        # the loop body of the reference Engine (BERT/src/engine.py:160-281); its own loop
-        # deletes an unbound name after the first batch on rank 0 (engine.py:197).  Returns
-        # the batch loss on the last rank: the reference's 1F1B turns every micro-batch loss
-        # into a host float (loss.item(), schedules.py:778-784), and the engine averages them.
+        # the loop body of the reference Engine (BERT/src/engine.py:160-281, Vit/src/engine.py);
+        # its own loop deletes an unbound name after the first batch on rank 0
+        # (BERT/src/engine.py:197).  Returns the batch loss on the last rank: the reference's
+        # 1F1B turns every micro-batch loss into a host float (loss.item(),
+        # schedules.py:778-784), and the engine averages them.
         b = host[i % 2]
         loss = None
         if rank == 0:
-            ids = b["ids"].to(dev, non_blocking=True)
-            mask = b["mask"].to(dev, non_blocking=True)
             lab = b["labels"].to(dev, non_blocking=True)
-            dist.isend(lab, dst=world - 1).wait()
-            sched.step(ids, mask)
+            if bert:
+                ids = b["ids"].to(dev, non_blocking=True)
+                mask = b["mask"].to(dev, non_blocking=True)
+                dist.isend(lab, dst=world - 1).wait()
+                sched.step(ids, mask)
+            else:
+                img = b["images"].to(dev, non_blocking=True)
+                dist.isend(lab, dst=world - 1).wait()
+                sched.step(img)
         elif rank == world - 1:
             dist.irecv(labels_buf, src=0).wait()
             losses = []
             sched.step(target=labels_buf, losses=losses)
-            loss = sum(losses) / len(losses)
+            loss = sum(float(x) for x in losses) / len(losses)
         else:
             sched.step()
         for p in model.parameters():
@@ -406,7 +462,7 @@ def run_reference(args):
     rec = base_record(args, world, "reference")
     rec.update({"value": args.global_batch / (ms_max / 1e3), "ms_per_step": ms_max, "e2e": e2e,
                 "peak_hbm_gib": peak, "clocks": clocks, "gpu_launches": 0,
-                "api": "pipelining.RevPipelineStageWithPareprop + Schedule1F1B (baseline/_ref/BERT)"})
+                "api": f"pipelining.{stage_cls.__name__} + Schedule1F1B (baseline/_ref/{'BERT' if bert else 'Vit'})"})
     if rank == 0:
         print(json.dumps(rec), flush=True)
     barrier(dev)

@@ -48,23 +48,33 @@ struct GemmArgs {
   const float* resid;  // [M, ld_resid] fp32 (kEpiResid)
   long long ld_resid;
   float sign;
-  float* colsum;  // [N] fp32 or null: kEpiDGelu adds the column sums of its (bf16) output
-  int chunked;    // 1: each CTA (pair) takes a contiguous run of tiles instead of every grid-th
+  float* colsum_part;  // [ceil(M/32), N] fp32 or null: kEpiDGelu writes the column sums of every
+                       // 32-row group of its (bf16) output there (reduced by gemm_colsum_reduce)
+  int raster_m;        // 1: tiles numbered m-fastest (kept for measurements); 0: n-fastest
   int* status;
 };
 
-// Tiles of one CTA (or CTA pair) `id` of `n`: either every n-th tile, or - with
-// `chunked` - a contiguous run, so consecutive tiles mostly share the output column block
-// (tiles are numbered m-fastest) and per-column partial sums can stay in registers.
-struct TileRange {
-  int begin, end, step;
+// Output tile of linear tile index t.  n-fastest (the default): the CTAs (pairs) of a
+// persistent grid run consecutive tiles at the same time, so they share a few row blocks of
+// A and all of B through L2, and A is read from DRAM about once.  m-fastest walks a whole
+// column of tiles first: with many column tiles A is re-read from DRAM once per column.
+struct TileCoord {
+  int tm, tn, ts;
 };
-__device__ __forceinline__ TileRange tile_range(const GemmArgs& a, int id, int n, int num_tiles) {
-  if (a.chunked) {
-    return {static_cast<int>((static_cast<long long>(id) * num_tiles) / n),
-            static_cast<int>((static_cast<long long>(id + 1) * num_tiles) / n), 1};
+__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t) {
+  TileCoord c;
+  if (a.raster_m) {
+    c.tm = t % a.tiles_m;
+    const int r = t / a.tiles_m;
+    c.tn = r % a.tiles_n;
+    c.ts = r / a.tiles_n;
+  } else {
+    c.tn = t % a.tiles_n;
+    const int r = t / a.tiles_n;
+    c.tm = r % a.tiles_m;
+    c.ts = r / a.tiles_m;
   }
-  return {id, num_tiles, n};
+  return c;
 }
 
 constexpr int kGemmBM = 128;
@@ -130,13 +140,46 @@ __device__ __forceinline__ void epi_copy_out(const uint8_t* stg, int lane, void*
   }
 }
 
+// Side input of an epilogue round (the fp32 residual of kEpiResid, the bf16 pre-activation
+// of kEpiDGelu): eight 16-byte units per lane, rows row0 + 4 i + lane / 8, read
+// row-contiguously like the stores.  Loaded one round ahead of its use, so the latency of
+// the global loads overlaps the previous round instead of stalling the warp.
+template <int EPI>
+struct EpiSide {
+  using T = uint4;
+};
+template <>
+struct EpiSide<kEpiResid> {
+  using T = float4;
+};
+template <int EPI>
+__device__ __forceinline__ constexpr bool epi_has_side() {
+  return EPI == kEpiResid || EPI == kEpiDGelu;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epi_load_side(const GemmArgs& a, int lane, int row0, int col0,
+                                              typename EpiSide<EPI>::T (&sd)[8]) {
+  const int col = col0 + (lane & 7) * EpiTraits<EPI>::kElemPerUnit;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = 4 * i + (lane >> 3);
+    const bool ok = row0 + rr < a.M && col < a.N;
+    if constexpr (EPI == kEpiResid) {
+      sd[i] = ok ? *reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row0 + rr) * a.ld_resid + col)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      sd[i] = ok ? *reinterpret_cast<const uint4*>(a.aux + static_cast<long long>(row0 + rr) * a.ld_aux + col)
+                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
 // One staged round: `r` holds kCols accumulator columns of this thread's row
-// (row0 + lane), starting at output column col0.
-// `cs` (kEpiDGelu with column sums): this lane's running sums of the 8 output columns it
-// stores in this round (rows differ between lanes; flushed by gemm_colsum_flush).
+// (row0 + lane), starting at output column col0; `sd` the round's side input.
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* stg, int lane, int row0, int col0,
-                                                    const uint32_t* r, float* cs = nullptr) {
+                                                    const uint32_t* r, const typename EpiSide<EPI>::T (&sd)[8]) {
   using T = EpiTraits<EPI>;
   constexpr int NC = T::kCols;
   float v[NC];
@@ -189,15 +232,7 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       epi_copy_out<2>(stg, lane, a.aux_out, a.ld_aux, row0, col0, a.M, a.N);
     }
   } else if constexpr (EPI == kEpiResid) {
-    // C = resid + sign * bf16(acc + bias); the residual is read row-contiguously
-    float4 x[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = 4 * i + (lane >> 3);
-      x[i] = (row0 + rr < a.M && col < a.N)
-                 ? *reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row0 + rr) * a.ld_resid + col)
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    // C = resid + sign * bf16(acc + bias)
 #pragma unroll
     for (int j = 0; j < NC; ++j) v[j] = bf16r(v[j]);
     epi_stage_row<false>(stg, lane, v);
@@ -209,43 +244,48 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
       if (row0 + rr < a.M && col < a.N) {
         *reinterpret_cast<float4*>(static_cast<float*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
-            make_float4(x[i].x + sg * __uint_as_float(w.x), x[i].y + sg * __uint_as_float(w.y),
-                        x[i].z + sg * __uint_as_float(w.z), x[i].w + sg * __uint_as_float(w.w));
+            make_float4(sd[i].x + sg * __uint_as_float(w.x), sd[i].y + sg * __uint_as_float(w.y),
+                        sd[i].z + sg * __uint_as_float(w.z), sd[i].w + sg * __uint_as_float(w.w));
       }
     }
   } else if constexpr (EPI == kEpiDGelu) {
-    // C = bf16(bf16(acc) * gelu'(aux)), aux = pre-activation, read row-contiguously
-    uint4 ua[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = 4 * i + (lane >> 3);
-      ua[i] = (row0 + rr < a.M && col < a.N)
-                  ? *reinterpret_cast<const uint4*>(a.aux + static_cast<long long>(row0 + rr) * a.ld_aux + col)
-                  : make_uint4(0u, 0u, 0u, 0u);
-    }
+    // C = bf16(bf16(acc) * gelu'(aux)), aux = pre-activation; with colsum_part, the column
+    // sums of this round's 32 rows go to row row0 / 32 of the partial-sum buffer
     epi_stage_row<true>(stg, lane, v);
     __syncwarp();
+    float cs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rr = 4 * i + (lane >> 3);
       const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
       if (row0 + rr < a.M && col < a.N) {
         const uint32_t wa[4] = {w.x, w.y, w.z, w.w};
-        const uint32_t xa[4] = {ua[i].x, ua[i].y, ua[i].z, ua[i].w};
+        const uint32_t xa[4] = {sd[i].x, sd[i].y, sd[i].z, sd[i].w};
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 g = unpack_bf16x2(wa[e]);
           const float2 pre = unpack_bf16x2(xa[e]);
           o[e] = pack_bf16x2(g.x * gelu_erf_grad(pre.x), g.y * gelu_erf_grad(pre.y));
-          if (cs != nullptr) {
-            const float2 r = unpack_bf16x2(o[e]);
-            cs[2 * e] += r.x;
-            cs[2 * e + 1] += r.y;
-          }
+          const float2 rs = unpack_bf16x2(o[e]);
+          cs[2 * e] += rs.x;
+          cs[2 * e + 1] += rs.y;
         }
         *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
             make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (a.colsum_part != nullptr) {  // warp-uniform
+      // lanes u, u + 8, u + 16, u + 24 hold the same 8 columns (different rows)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 8);
+        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 16);
+      }
+      if (lane < 8 && row0 < a.M && col < a.N) {
+        float* dst = a.colsum_part + static_cast<long long>(row0 >> 5) * a.N + col;
+        *reinterpret_cast<float4*>(dst) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(cs[4], cs[5], cs[6], cs[7]);
       }
     }
   } else if constexpr (EPI == kEpiAtomicF32) {
@@ -264,84 +304,49 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
   __syncwarp();  // the staging tile is rewritten by the next round
 }
 
+// TMEM -> registers for one round (RC = 32 or 64 columns).
+template <int RC>
+__device__ __forceinline__ void epi_tmem_round(uint32_t taddr, uint32_t (&r)[RC]) {
+  tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+  if constexpr (RC == 64) tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+  tmem_wait_ld();
+}
+
 // The epilogue of one warp for one tile: WARP_COLS accumulator columns starting at TMEM
 // address `taddr` (lane quarter and column already applied), output rows row0..row0+31,
-// output columns from col0.
+// output columns from col0.  Epilogues with a side input run two rounds per iteration
+// with ping-pong side buffers, each loaded a round ahead.
 template <int EPI, int WARP_COLS>
 __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
                                                    int row0, int col0) {
   constexpr int RC = EpiTraits<EPI>::kCols;
+  using SideT = typename EpiSide<EPI>::T;
+  if constexpr (epi_has_side<EPI>()) {
+    SideT s0[8], s1[8];
+    epi_load_side<EPI>(a, lane, row0, col0, s0);
 #pragma unroll 1
-  for (int c = 0; c < WARP_COLS; c += RC) {
-    if (col0 + c >= a.N) break;  // warp-uniform
-    uint32_t r[RC];
-    tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-    if constexpr (RC == 64) tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-    tmem_wait_ld();
-    gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r);
-  }
-}
-
-// GELU-backward epilogue with bias-gradient column sums: as above, but each lane adds the
-// columns it stores into cs[round][8], kept in registers across the consecutive tiles of
-// one output column block.  One flush (shuffle reduction + one atomic per column and warp)
-// per column block replaces an atomic per column, warp and round of every tile: with 32
-// row tiles per column block sharing 256 addresses, those atomics serialised in L2 and
-// cost more than the GEMM itself (76 -> 122 us at 8192 x 4096 x 1024).
-template <int WARP_COLS>
-__device__ __forceinline__ void gemm_epilogue_warp_dgelu_cs(const GemmArgs& a, uint8_t* stg, int lane,
-                                                            uint32_t taddr, int row0, int col0,
-                                                            float (&cs)[WARP_COLS / 64][8]) {
-#pragma unroll
-  for (int rd = 0; rd < WARP_COLS / 64; ++rd) {
-    if (col0 + rd * 64 >= a.N) break;  // warp-uniform
-    uint32_t r[64];
-    tmem_ld32(taddr + rd * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-    tmem_ld32(taddr + rd * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-    tmem_wait_ld();
-    gemm_epilogue_round<kEpiDGelu>(a, stg, lane, row0, col0 + rd * 64, r, cs[rd]);
-  }
-}
-
-// Adds the column sums held in cs (columns col0 .. col0 + WARP_COLS of this warp's rows)
-// to a.colsum and clears them.  Lanes u, u + 8, u + 16, u + 24 hold the same 8 columns.
-template <int WARP_COLS>
-__device__ __forceinline__ void gemm_colsum_flush(const GemmArgs& a, int lane, int col0,
-                                                  float (&cs)[WARP_COLS / 64][8]) {
-#pragma unroll
-  for (int rd = 0; rd < WARP_COLS / 64; ++rd) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      cs[rd][e] += __shfl_xor_sync(0xffffffffu, cs[rd][e], 8);
-      cs[rd][e] += __shfl_xor_sync(0xffffffffu, cs[rd][e], 16);
+    for (int c = 0; c < WARP_COLS; c += 2 * RC) {
+      if (col0 + c >= a.N) break;  // warp-uniform
+      const bool more1 = c + RC < WARP_COLS && col0 + c + RC < a.N;
+      if (more1) epi_load_side<EPI>(a, lane, row0, col0 + c + RC, s1);
+      uint32_t r[RC];
+      epi_tmem_round<RC>(taddr + c, r);
+      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r, s0);
+      if (!more1) break;
+      if (c + 2 * RC < WARP_COLS && col0 + c + 2 * RC < a.N) epi_load_side<EPI>(a, lane, row0, col0 + c + 2 * RC, s0);
+      epi_tmem_round<RC>(taddr + c + RC, r);
+      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c + RC, r, s1);
     }
-    const int col = col0 + rd * 64 + (lane & 7) * 8;
-    if (lane < 8 && col < a.N) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) atomicAdd(a.colsum + col + e, cs[rd][e]);
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) cs[rd][e] = 0.f;
-  }
-}
-
-// One warp's share of one output tile.  With kEpiDGelu and column sums, `cs` carries the
-// column sums of column block `cs_tn` across tiles; a new column block flushes them first.
-template <int EPI, int WARP_COLS>
-__device__ __forceinline__ void gemm_epilogue_tile(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
-                                                   int row0, int col0, int tn, float (&cs)[WARP_COLS / 64][8],
-                                                   int& cs_tn) {
-  if constexpr (EPI == kEpiDGelu) {
-    if (a.colsum != nullptr) {  // warp-uniform
-      if (tn != cs_tn) {
-        if (cs_tn >= 0) gemm_colsum_flush<WARP_COLS>(a, lane, col0 + (cs_tn - tn) * kGemmColGroups * WARP_COLS, cs);
-        cs_tn = tn;
-      }
-      gemm_epilogue_warp_dgelu_cs<WARP_COLS>(a, stg, lane, taddr, row0, col0, cs);
-      return;
+  } else {
+    const SideT none[8] = {};
+#pragma unroll 1
+    for (int c = 0; c < WARP_COLS; c += RC) {
+      if (col0 + c >= a.N) break;  // warp-uniform
+      uint32_t r[RC];
+      epi_tmem_round<RC>(taddr + c, r);
+      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r, none);
     }
   }
-  gemm_epilogue_warp<EPI, WARP_COLS>(a, stg, lane, taddr, row0, col0);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
-  const TileRange trange = tile_range(args, blockIdx.x, gridDim.x, num_tiles);
+  const int t_first = blockIdx.x, t_step = gridDim.x;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -410,12 +415,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, issued_parity = 0;  // per-stage bits, for the drain on abort
-      for (int t = trange.begin; t < trange.end; t += trange.step) {
-        const int tm = t % args.tiles_m;
-        const int rest = t / args.tiles_m;
-        const int tn = rest % args.tiles_n;
-        const int ts = rest / args.tiles_n;
-        const int kb0 = ts * args.kb_per_split;
+      for (int t = t_first; t < num_tiles; t += t_step) {
+        const TileCoord tc = tile_coord(args, t);
+        const int tm = tc.tm, tn = tc.tn;
+        const int kb0 = tc.ts * args.kb_per_split;
         const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, abort_flag)) goto producer_abort;
@@ -466,10 +469,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t acc_phase = 0;
       const uint32_t a_base = smem_u32(sA);
       const uint32_t b_base = smem_u32(sB);
-      for (int t = trange.begin; t < trange.end; t += trange.step) {
-        const int rest = t / args.tiles_m;
-        const int ts = rest / args.tiles_n;
-        const int kb0 = ts * args.kb_per_split;
+      for (int t = t_first; t < num_tiles; t += t_step) {
+        const int kb0 = tile_coord(args, t).ts * args.kb_per_split;
         const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, abort_flag)) break;
         tc_fence_after();
@@ -515,17 +516,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int cg = ew >> 2;     // column half handled by this warp
     int acc = 0;
     uint32_t acc_phase = 0;
-    float cs[BN / kGemmColGroups / 64][8] = {};  // kEpiDGelu column sums of the current column block
-    int cs_tn = -1;
-    for (int t = trange.begin; t < trange.end; t += trange.step) {
-      const int tm = t % args.tiles_m;
-      const int tn = (t / args.tiles_m) % args.tiles_n;
+    for (int t = t_first; t < num_tiles; t += t_step) {
+      const TileCoord tc = tile_coord(args, t);
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
-      gemm_epilogue_tile<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tm * BM + q * 32,
-                                      tn * BN + cg * (BN / kGemmColGroups), tn, cs, cs_tn);
+      gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tc.tm * BM + q * 32,
+                                                   tc.tn * BN + cg * (BN / kGemmColGroups));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -533,9 +531,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
-    }
-    if constexpr (EPI == kEpiDGelu) {
-      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / kGemmColGroups>(args, lane, cs_tn * BN + cg * (BN / kGemmColGroups), cs);
     }
   }
 
@@ -621,7 +616,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
-  const TileRange trange = tile_range(args, cluster_id, num_clusters, num_tiles);
+  const int t_first = cluster_id, t_step = num_clusters;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -630,12 +625,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0, issued_parity = 0;
       const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
-      for (int t = trange.begin; t < trange.end; t += trange.step) {
-        const int tm = t % args.tiles_m;
-        const int rest = t / args.tiles_m;
-        const int tn = rest % args.tiles_n;
-        const int ts = rest / args.tiles_n;
-        const int kb0 = ts * args.kb_per_split;
+      for (int t = t_first; t < num_tiles; t += t_step) {
+        const TileCoord tc = tile_coord(args, t);
+        const int tm = tc.tm, tn = tc.tn;
+        const int kb0 = tc.ts * args.kb_per_split;
         const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
         const int a_row0 = tm * 2 * BM + crank * BM;
         const int b_row0 = tn * BN + crank * HALF_N;
@@ -693,10 +686,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t acc_phase = 0;
       const uint32_t a_base = smem_u32(sA);
       const uint32_t b_base = smem_u32(sB);
-      for (int t = trange.begin; t < trange.end; t += trange.step) {
-        const int rest = t / args.tiles_m;
-        const int ts = rest / args.tiles_n;
-        const int kb0 = ts * args.kb_per_split;
+      for (int t = t_first; t < num_tiles; t += t_step) {
+        const int kb0 = tile_coord(args, t).ts * args.kb_per_split;
         const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, abort_flag)) break;
         tc_fence_after();
@@ -745,17 +736,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    float cs[BN / kGemmColGroups / 64][8] = {};  // kEpiDGelu column sums of the current column block
-    int cs_tn = -1;
-    for (int t = trange.begin; t < trange.end; t += trange.step) {
-      const int tm = t % args.tiles_m;
-      const int tn = (t / args.tiles_m) % args.tiles_n;
+    for (int t = t_first; t < num_tiles; t += t_step) {
+      const TileCoord tc = tile_coord(args, t);
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
-      gemm_epilogue_tile<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
-                                      tm * 2 * BM + crank * BM + q * 32, tn * BN + cg * (BN / kGemmColGroups), tn, cs, cs_tn);
+      gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
+                                                   tc.tm * 2 * BM + crank * BM + q * 32,
+                                                   tc.tn * BN + cg * (BN / kGemmColGroups));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
@@ -763,9 +752,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
-    }
-    if constexpr (EPI == kEpiDGelu) {
-      if (args.colsum != nullptr && cs_tn >= 0) gemm_colsum_flush<BN / kGemmColGroups>(args, lane, cs_tn * BN + cg * (BN / kGemmColGroups), cs);
     }
   }
 
@@ -777,6 +763,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_dealloc2(tmem_base, TMEM_COLS);
   }
   cluster_sync();
+}
+
+// colsum[n] += sum_r part[r, n] over the partial column sums of the GELU-backward epilogue.
+// Block (x, y): 128 columns (a float4 per lane), rows y, y + gridDim.y, ... split over 8
+// warps; one float4 atomic per lane and block row-group.
+__global__ void __launch_bounds__(256) gemm_colsum_reduce_kernel(const float* __restrict__ part,
+                                                                  float* __restrict__ colsum, int rows, int N) {
+  __shared__ float4 red[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = blockIdx.x * 128 + lane * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col < N) {
+    for (int r = blockIdx.y + gridDim.y * warp; r < rows; r += gridDim.y * 8) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(part + static_cast<long long>(r) * N + col));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && col < N) {
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 v = red[w][lane];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    atomicAdd(reinterpret_cast<float4*>(colsum + col), acc);
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -963,20 +976,22 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
     args.ld_resid = resid->stride(0);
   }
   args.sign = static_cast<float>(sign);
-  args.colsum = nullptr;
+  args.colsum_part = nullptr;
+  torch::Tensor part;
   if (colsum.has_value() && colsum->defined()) {
     REVPP_CHECK(epi == kEpiDGelu, "the fused column sum is implemented for the GELU-backward epilogue only");
     check_cuda_f32(*colsum, "colsum");
     REVPP_CHECK(colsum->is_contiguous() && colsum->numel() >= N, "colsum must hold N floats");
-    args.colsum = colsum->data_ptr<float>();
+    // one row of partial column sums per 32 output rows, every row written by the epilogue
+    part = torch::empty({(M + 31) / 32, N}, colsum->options());
+    args.colsum_part = part.data_ptr<float>();
   }
-  // Contiguous tile runs keep the column-sum partials of the GELU-backward epilogue in
-  // registers; REVPP_GEMM_CHUNKED=1 / 0 forces the order for every GEMM (measurements).
-  static const int chunk_env = [] {
-    const char* e = std::getenv("REVPP_GEMM_CHUNKED");
-    return e == nullptr ? -1 : std::atoi(e);
+  // REVPP_GEMM_RASTER=m numbers tiles m-fastest (the older order), for measurements
+  static const int raster_m = [] {
+    const char* e = std::getenv("REVPP_GEMM_RASTER");
+    return (e != nullptr && e[0] == 'm') ? 1 : 0;
   }();
-  args.chunked = chunk_env >= 0 ? (chunk_env != 0) : (args.colsum != nullptr);
+  args.raster_m = raster_m;
   args.status = status_device_ptr();
 
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -995,6 +1010,13 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
   } else {
     const int grid = std::min(num_tiles, gemm_grid_sms());
     dispatch_gemm(a_mn, b_mn, static_cast<int>(epi), ta, tb, args, grid, st);
+  }
+  if (args.colsum_part != nullptr) {
+    const int rows = static_cast<int>((M + 31) / 32);
+    dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(std::min(8, rows)));
+    gemm_colsum_reduce_kernel<<<grid, 256, 0, st>>>(args.colsum_part, colsum->data_ptr<float>(), rows,
+                                                    static_cast<int>(N));
+    REVPP_CHECK_LAUNCH();
   }
 }
 

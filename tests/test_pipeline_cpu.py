@@ -232,3 +232,54 @@ def test_copy_channels_match_autograd(extra, world):
     cfg = _cfg(extra, world)
     v = cfg.virtual_stages if cfg.schedule == "interleaved" else 1
     _check(gathered, cfg, world, v)
+
+
+def _train_worker(rank, world, port, extra, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        args = parse_args(("--preset tiny-bert --num-hidden-layers 2 --batch-size 8 --microbatch-size 4 "
+                           "--num-microbatches 2 --device cpu --lr 1e-2 --reversible " + extra).split())
+        cfg = build_global_config(args)
+        env = build_env(cfg, timeout_s=120)
+        set_seed(cfg.seed)
+        tr = Trainer(cfg, env)
+        batch = SyntheticBatches(cfg, tr.local_batch, 1, seed=300 + rank).make(0)
+        for _ in range(2):
+            tr.train_step(batch)
+        out = (tr.flat.data.clone().numpy(), int(tr.flat.exp_avg.numel()), int(tr.flat.numel))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, out)
+        if rank == 0:
+            q.put(("ok", gathered))
+        env.close()
+    except Exception:  # noqa: BLE001
+        import traceback
+
+        q.put(("err", f"rank {rank}: {traceback.format_exc()}"))
+        raise
+
+
+def _run_train(extra, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_train_worker, args=(r, world, port, extra, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    status, payload = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+    assert status == "ok", payload
+    return payload
+
+
+def test_fsdp_shards_adam_state_and_matches_ddp():
+    """--par-mode fsdp (ZeRO-2): each rank holds Adam moments of its half only, and two
+    steps leave the same parameters as --par-mode ddp, identical on both ranks."""
+    fsdp = _run_train("--par-mode fsdp")
+    ddp = _run_train("--par-mode ddp")
+    for (p, n_m, n), (pd, n_md, _) in zip(fsdp, ddp):
+        assert n_m == n // 2 and n_md == n
+        assert abs(p - pd).max() < 1e-5, abs(p - pd).max()
+    assert (fsdp[0][0] == fsdp[1][0]).all()
