@@ -39,6 +39,8 @@ void scale_(torch::Tensor x, double s);
 // attention_tc.cu
 void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
                  int64_t heads, const c10::optional<torch::Tensor>& phase_ns);
+void attn_fwd_persistent(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
+                         int64_t heads);
 // comm.cu
 void dp_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
                      const std::vector<int64_t>& shadow_ptrs, const std::vector<int64_t>& flag_ptrs, torch::Tensor m,
@@ -115,6 +117,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dx_f32") = py::none(), py::arg("dx_bf16") = py::none(), py::arg("colsum") = py::none());
   m.def("attn_fwd", &revpp::attn_fwd, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"),
         py::arg("heads"));
+  m.def("attn_fwd_persistent", &revpp::attn_fwd_persistent, "persistent tcgen05 flash attention forward",
+        py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"), py::arg("heads"));
   m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("heads"), py::arg("phase_ns") = py::none());
   m.def("attn_bwd_tc", &revpp::attn_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),

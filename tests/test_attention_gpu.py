@@ -58,16 +58,22 @@ def test_attn_fwd_bwd(B, S, heads):
     assert C.status_read_and_clear() == 0
 
 
+FWD_KERNELS = ["attn_fwd_tc", "attn_fwd_persistent"]
+
+
+@pytest.mark.parametrize("kernel", FWD_KERNELS)
 @pytest.mark.parametrize("B,S,heads", [(1, 64, 1), (2, 197, 2), (2, 512, 16), (3, 577, 4), (1, 100, 3), (1, 150, 2),
-                                       (1, 2048, 2)])
-def test_attn_fwd_tcgen05(B, S, heads):
-    """tcgen05 forward against float64 attention and against the mma.sync kernel."""
+                                       (1, 2048, 2), (20, 577, 8), (40, 512, 16)])
+def test_attn_fwd_tcgen05(B, S, heads, kernel):
+    """tcgen05 forward kernels against float64 attention and against the mma.sync kernel.
+    The last two shapes give the persistent kernel several work items per CTA, some with
+    a second query tile past the sequence end."""
     C = _C()
     H = heads * 64
     qkv = (torch.randn(B * S, 3 * H, device="cuda") * 1.5).to(torch.bfloat16)
     out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, heads, S, device="cuda")
-    C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+    getattr(C, kernel)(qkv, out, lse, B, S, heads)
     out2 = torch.empty_like(out)
     lse2 = torch.empty_like(lse)
     C.attn_fwd(qkv, out2, lse2, B, S, heads)
@@ -112,8 +118,9 @@ def test_attn_bwd_tcgen05(B, S, heads):
     assert (dqkv.double() - dqkv2.double()).abs().max().item() < 3e-2 * scale
 
 
+@pytest.mark.parametrize("kernel", FWD_KERNELS)
 @pytest.mark.parametrize("B,S,heads", [(1, 512, 2), (2, 577, 1)])
-def test_attn_fwd_tcgen05_rising_scores(B, S, heads):
+def test_attn_fwd_tcgen05_rising_scores(B, S, heads, kernel):
     """Scores that grow along the keys: the row maximum rises by far more than the
     rescale threshold from one 64-key tile to the next, so the kernel's in-TMEM output
     rescale runs for every row on most tiles."""
@@ -126,7 +133,7 @@ def test_attn_fwd_tcgen05_rising_scores(B, S, heads):
     qkv = x.reshape(B * S, 3 * H).to(torch.bfloat16)
     out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, heads, S, device="cuda")
-    C.attn_fwd_tc(qkv, out, lse, B, S, heads)
+    getattr(C, kernel)(qkv, out, lse, B, S, heads)
     torch.cuda.synchronize()
     assert C.status_read_and_clear() == 0
     o_ref, lse_ref = _ref(qkv.double(), B, S, heads)
