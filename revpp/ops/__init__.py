@@ -72,19 +72,19 @@ def cast_colsum(inp, out=None, colsum=None):
 
 
 _ATTN_TC = os.environ.get("REVPP_ATTN_TC", "1") != "0"
-_ATTN_FWD = os.environ.get("REVPP_ATTN_FWD", "persistent")
+_ATTN_FWD = os.environ.get("REVPP_ATTN_FWD", "grid")
 
 
 def attention_fwd(qkv, out, lse, B, S, heads):
-    """Flash attention forward: the persistent tcgen05 kernel (REVPP_ATTN_FWD=grid selects
-    the one-CTA-per-query-tile tcgen05 kernel, REVPP_ATTN_TC=0 the warp-level mma.sync
-    kernel; both kept as comparison points)."""
+    """Flash attention forward: the tcgen05 kernel with one CTA per query tile, two CTAs per
+    SM (REVPP_ATTN_FWD=persistent selects the persistent kernel, measured slower at head
+    dim 64; REVPP_ATTN_TC=0 the warp-level mma.sync kernel; both kept as comparison points)."""
     if not _ATTN_TC:
         ext().attn_fwd(qkv, out, lse, B, S, heads)
-    elif _ATTN_FWD == "grid":
-        ext().attn_fwd_tc(qkv, out, lse, B, S, heads)
-    else:
+    elif _ATTN_FWD == "persistent":
         ext().attn_fwd_persistent(qkv, out, lse, B, S, heads)
+    else:
+        ext().attn_fwd_tc(qkv, out, lse, B, S, heads)
 
 
 def attention_bwd(qkv, out, dout, lse, dqkv, dq_acc, dbuf, B, S, heads, colsum=None):

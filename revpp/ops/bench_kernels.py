@@ -82,7 +82,7 @@ def bench_attn(a, C, backward: bool):
     qkv = torch.randn(B * S, 3 * H, device="cuda").to(torch.bfloat16)
     out = torch.empty(B * S, H, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, heads, S, device="cuda")
-    fwd = C.attn_fwd_tc if a.impl == "tc" else C.attn_fwd
+    fwd = {"persistent": C.attn_fwd_persistent, "tc": C.attn_fwd_tc, "mma": C.attn_fwd}[a.impl]
     fwd(qkv, out, lse, B, S, heads)
     flops = 4.0 * B * S * S * H
     if not backward:
@@ -93,8 +93,9 @@ def bench_attn(a, C, backward: bool):
     dqkv = torch.empty_like(qkv)
     dq = torch.empty(B * S, H, device="cuda")
     D = torch.empty(B, heads, S, device="cuda")
-    bwd = C.attn_bwd_tc if a.impl == "tc" else C.attn_bwd
-    if a.impl == "tc":  # with the fused q/k/v bias-gradient column sums, as in training
+    tc = a.impl in ("tc", "persistent")
+    bwd = C.attn_bwd_tc if tc else C.attn_bwd
+    if tc:  # with the fused q/k/v bias-gradient column sums, as in training
         cs = torch.zeros(3 * H, device="cuda")
         ms = _time(lambda: bwd(qkv, out, dout, lse, dqkv, dq, D, B, S, heads, colsum=cs), a.warmup, a.iters)
     else:
@@ -238,7 +239,8 @@ def main(argv=None):
     p.add_argument("--B", type=int, default=16)
     p.add_argument("--S", type=int, default=512)
     p.add_argument("--heads", type=int, default=16)
-    p.add_argument("--impl", choices=["tc", "mma"], default="tc")
+    p.add_argument("--impl", choices=["persistent", "tc", "mma"], default="tc",
+                   help="attention kernels: persistent / one-CTA-per-tile tcgen05 forward, or mma.sync")
     p.add_argument("--cublas", action="store_true", help="gemm: time torch.matmul on the same shape instead")
     p.add_argument("--n", type=int, default=335_000_000)
     p.add_argument("--warmup", type=int, default=3)
