@@ -672,8 +672,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         // softmax of tile j is done: P^T of tile j is in TMEM, dS^T in buffer pb
         if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
-        tc_fence_after();
-        if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
         if (j < 4) phase_stamp(args.phase_ns, 8 + 4 * j + 3);  // tile j's gradient MMAs issued
         tc_fence_after();
         const uint32_t a_dsj = a_ds + pb * kSqTile;
@@ -692,6 +690,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16_ss(tmem + 320, sdesc_sw128(a_dsj + ka, 16, 1024),
                        sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
         }
+        // the dQ warps have read the previous tile's dQ from TMEM (dV / dK above need not wait)
+        if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
+        tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           // dQ = dS K : A = dS (queries contiguous in the dS^T tile -> MN-major, 64-query
@@ -753,16 +754,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (j == 0 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 2);  // first S^T / dP^T ready
       if (j < 4 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 8 + 4 * j + 0);  // tile j: softmax starts
-      if (!mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag)) {
-        ok = false;
-        break;
-      }
-      // P^T of the previous tile has been read by its dV MMAs (warp-uniform: tcgen05.st
-      // below is a warp-wide instruction)
-      if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pt_free, (j - 1) & 1, args.status, abort_flag))) {
-        ok = false;
-        break;
-      }
       tc_fence_after();
       const int sw = r & 7;
       // the dS^T tile is two 64-query swizzle chunks; this group's queries start at 16-byte
@@ -785,6 +776,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         const int q4 = 4 * k;  // first float4 of this sub-chunk's LSE / D in the warp's copy
         uint32_t pw[8], dw[8];
+        bool waited = true;
         if (key_ok) {
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
@@ -807,6 +799,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) pw[e] = dw[e] = 0u;
         }
+        if (k == 0) {
+          // only the stores wait: the dS^T buffer must have been read by the gradient MMAs of
+          // tile j - 2, and P^T of the previous tile by its dV MMAs (warp-uniform: tcgen05.st
+          // is a warp-wide instruction); the first sub-chunk's exponentials overlap those MMAs
+          waited = mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag);
+          if (j > 0) waited = waited && mbar_wait(pt_free, (j - 1) & 1, args.status, abort_flag);
+          waited = __all_sync(0xffffffffu, waited);
+          tc_fence_after();
+        }
+        if (!waited) {
+          ok = false;
+          break;
+        }
         // P^T: the 16 queries are TMEM columns kTmemPt + (qb + 16k) / 2 .. + 7 of this key's lane
         tmem_st8(tmem + lane_off + kTmemPt + qb / 2 + 8 * k, pw);
         // dS^T: 16 queries = 32 bytes = 16-byte units u0 + 2k, u0 + 2k + 1 of this row
@@ -816,6 +821,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
         }
       }
+      if (!ok) break;
       tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
