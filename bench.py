@@ -47,6 +47,9 @@ import torch.distributed as dist
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train samples/sec + peak HBM/GPU, Rev-BERT-Large PaBER at PP=1/2/4/8 vs ref"
 MODEL = dict(hidden=1024, heads=16, layers=24, seq=512, vocab=30522, classes=2)
+# defaults of the revpp arm with several pipeline stages
+DEFAULT_P2P = "group"
+DEFAULT_SCHEDULE = "1f1b"
 
 
 def parse():
@@ -71,7 +74,7 @@ def parse():
     p.add_argument("--virtual-stages", type=int, default=None,
                    help="model chunks per rank with the interleaved schedule (default: one block per chunk "
                         "up to 3 chunks)")
-    p.add_argument("--p2p", choices=["auto", "copy", "group"], default="auto",
+    p.add_argument("--p2p", choices=["auto", "copy", "group"], default=DEFAULT_P2P,
                    help="stage messages: copy-engine channels or NCCL groups (revpp arm)")
     a = p.parse_args()
     if a.model != "bert-large" and a.layers == MODEL["layers"]:
@@ -82,7 +85,7 @@ def parse():
         a.microbatch_size = 64 if a.gpus // a.dp == 1 else 16
     P = a.gpus // a.dp
     if a.schedule is None:
-        a.schedule = "interleaved" if (P > 1 and a.impl == "revpp" and a.p2p != "group") else "1f1b"
+        a.schedule = DEFAULT_SCHEDULE if (P > 1 and a.impl == "revpp" and a.p2p != "group") else "1f1b"
     if a.virtual_stages is None:
         a.virtual_stages = default_virtual_stages(a, P)
     if a.schedule != "interleaved":
