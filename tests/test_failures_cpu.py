@@ -18,7 +18,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, env_extra, q):
+def _worker(rank, world, port, env_extra, q, extra_args=""):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), REVPP_P2P_HOST_TIMEOUT_S="8", **env_extra)
     import torch
@@ -30,8 +30,8 @@ def _worker(rank, world, port, env_extra, q):
     from revpp.utils.seed import set_seed
 
     try:
-        args = parse_args("--preset tiny-bert --num-hidden-layers 2 --reversible --par-mode pp --batch-size 8 "
-                          "--microbatch-size 2 --num-microbatches 4 --device cpu".split())
+        args = parse_args(("--preset tiny-bert --num-hidden-layers 2 --reversible --par-mode pp --batch-size 8 "
+                           "--microbatch-size 2 --num-microbatches 4 --device cpu " + extra_args).split())
         cfg = build_global_config(args)
         env = build_env(cfg, timeout_s=8)
         set_seed(rank)
@@ -44,11 +44,11 @@ def _worker(rank, world, port, env_extra, q):
         q.put((rank, f"error:{type(e).__name__}", 0.0))
 
 
-def _run(env_extra, timeout=90):
+def _run(env_extra, timeout=90, extra_args=""):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, env_extra, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, env_extra, q, extra_args)) for r in range(2)]
     t0 = time.time()
     for p in procs:
         p.start()
@@ -85,6 +85,27 @@ def test_rank_raises_peer_fails_fast():
 def test_dropped_message_times_out():
     res, dt = _run({"REVPP_FAULT_DROP_SEND": "fwd0->1:1"})
     assert res.get(1, "").startswith("error"), res
+    assert dt < 80
+
+
+def test_copy_channels_clean_run_and_raising_rank():
+    """Over copy channels: a clean step completes; a rank that raises mid-step marks the
+    shared abort word, so its peer's next channel wait raises at once instead of waiting
+    out the host time limit (8 s here)."""
+    res, _ = _run({}, extra_args="--p2p copy")
+    assert res == {0: "ok", 1: "ok"}
+    res, dt = _run({"REVPP_FAULT_RAISE_AT": "1:1"}, extra_args="--p2p copy")
+    assert res.get(1, "").startswith("error:InjectedFault"), res
+    assert res.get(0, "").startswith("error:ChannelError"), res
+    assert dt < 60
+
+
+def test_copy_channels_rank_exit_peer_times_out():
+    """A rank that exits without a word leaves its peer waiting on a channel until the host
+    time limit, which then raises."""
+    res, dt = _run({"REVPP_FAULT_EXIT_AT": "0:2"}, extra_args="--p2p copy")
+    assert 0 not in res or res[0] != "ok"
+    assert res.get(1, "").startswith("error:ChannelError"), res
     assert dt < 80
 
 
