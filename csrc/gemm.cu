@@ -175,6 +175,25 @@ __device__ __forceinline__ void epi_load_side(const GemmArgs& a, int lane, int r
   }
 }
 
+// L2 prefetch of the side input of a warp's next tile (rows row0 .. row0 + 31, columns
+// col0 .. col0 + ncols): one 128-byte line per row and round, issued by the lane of that row,
+// no registers held.  The register prefetch one round ahead then finds the lines in L2.
+template <int EPI, int WARP_COLS>
+__device__ __forceinline__ void epi_prefetch_side_l2(const GemmArgs& a, int lane, int row0, int col0) {
+  const int row = row0 + lane;
+  if (row >= a.M) return;
+  constexpr int kRowBytes = WARP_COLS * (EPI == kEpiResid ? 4 : 2);
+#pragma unroll
+  for (int b = 0; b < kRowBytes / 128; ++b) {
+    const int col = col0 + b * (EPI == kEpiResid ? 32 : 64);
+    if (col >= a.N) break;
+    const void* p = EPI == kEpiResid
+                        ? static_cast<const void*>(a.resid + static_cast<long long>(row) * a.ld_resid + col)
+                        : static_cast<const void*>(a.aux + static_cast<long long>(row) * a.ld_aux + col);
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+  }
+}
+
 // One staged round: `r` holds kCols accumulator columns of this thread's row
 // (row0 + lane), starting at output column col0; `sd` the round's side input.
 template <int EPI>
@@ -318,10 +337,11 @@ __device__ __forceinline__ void epi_tmem_round(uint32_t taddr, uint32_t (&r)[RC]
 // with ping-pong side buffers, each loaded a round ahead.
 template <int EPI, int WARP_COLS>
 __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
-                                                   int row0, int col0) {
+                                                   int row0, int col0, int next_row0 = -1, int next_col0 = 0) {
   constexpr int RC = EpiTraits<EPI>::kCols;
   using SideT = typename EpiSide<EPI>::T;
   if constexpr (epi_has_side<EPI>()) {
+    if (next_row0 >= 0) epi_prefetch_side_l2<EPI, WARP_COLS>(a, lane, next_row0, next_col0);
     SideT s0[8], s1[8];
     epi_load_side<EPI>(a, lane, row0, col0, s0);
 #pragma unroll 1
@@ -522,8 +542,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+      int nrow = -1, ncol = 0;
+      if (t + t_step < num_tiles) {
+        const TileCoord nc = tile_coord(args, t + t_step);
+        nrow = nc.tm * BM + q * 32;
+        ncol = nc.tn * BN + cg * (BN / kGemmColGroups);
+      }
       gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tc.tm * BM + q * 32,
-                                                   tc.tn * BN + cg * (BN / kGemmColGroups));
+                                                   tc.tn * BN + cg * (BN / kGemmColGroups), nrow, ncol);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -742,9 +768,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+      int nrow = -1, ncol = 0;
+      if (t + t_step < num_tiles) {
+        const TileCoord nc = tile_coord(args, t + t_step);
+        nrow = nc.tm * 2 * BM + crank * BM + q * 32;
+        ncol = nc.tn * BN + cg * (BN / kGemmColGroups);
+      }
       gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
                                                    tc.tm * 2 * BM + crank * BM + q * 32,
-                                                   tc.tn * BN + cg * (BN / kGemmColGroups));
+                                                   tc.tn * BN + cg * (BN / kGemmColGroups), nrow, ncol);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
