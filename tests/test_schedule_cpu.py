@@ -70,3 +70,48 @@ def test_recv_ring_detects_reuse_before_consume():
     s2, b2 = ring.acquire()
     assert s2 == s0 and b2[0].data_ptr() == b0[0].data_ptr()
     assert ring.gen[s0] == 2
+
+
+@pytest.mark.parametrize("P,v,n", [(2, 2, 8), (4, 2, 8), (4, 3, 32), (8, 3, 32), (4, 2, 4)])
+def test_interleaved_order(P, v, n):
+    """Every rank runs the forward and the backward of every (chunk, micro-batch) exactly
+    once, each forward before its backward, with the reference's warm-up length."""
+    from revpp.parallel.schedule import interleaved_1f1b
+
+    for r in range(P):
+        acts = interleaved_1f1b(r, P, v, n)
+        want = sorted((c, m) for c in range(v) for m in range(n))
+        assert sorted((c, m) for k, c, m in acts if k == "F") == want
+        assert sorted((c, m) for k, c, m in acts if k == "B") == want
+        for c in range(v):
+            for m in range(n):
+                assert acts.index(("F", c, m)) < acts.index(("B", c, m))
+        warm = n * v if n == P else min((P - r - 1) * 2 + (v - 1) * P, n * v)
+        assert all(k == "F" for k, _, _ in acts[:warm]) and acts[warm][0] == "F" or warm == n * v
+
+
+def test_interleaved_reduces_bubble():
+    """The simulated makespan of interleaved 1F1B beats plain 1F1B at the same work, and the
+    gain grows with the pipeline depth."""
+    from revpp.parallel.schedule import simulate_virtual
+
+    gains = []
+    for P in (2, 4, 8):
+        base, _ = simulate_virtual(P, 1, 32, "1f1b", 1.0, 3.0)
+        il, busy = simulate_virtual(P, 3, 32, "interleaved", 1.0 / 3, 1.0)
+        assert il < base
+        assert abs(sum(busy) / P - 32 * 4.0) < 1e-6  # same work per rank
+        gains.append(base / il)
+    assert gains == sorted(gains)
+
+
+@pytest.mark.parametrize("P,v", [(2, 1), (4, 1), (8, 1), (2, 2), (4, 3), (8, 3)])
+def test_channel_depth_is_deadlock_free_and_minimal(P, v):
+    """The host-level run of the channel protocol finishes two steps with the chosen ring
+    depth (and with a deeper ring)."""
+    from revpp.parallel.schedule import host_deadlock_free, min_channel_depth
+
+    sched = "interleaved" if v > 1 else "1f1b"
+    d = min_channel_depth(P, v, 32, sched)
+    assert host_deadlock_free(P, v, 32, sched, d)
+    assert host_deadlock_free(P, v, 32, sched, d + 1)
