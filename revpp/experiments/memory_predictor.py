@@ -7,8 +7,10 @@ Per parameter: fp32 master + fp32 gradient + two fp32 Adam moments + bf16 shadow
 Activations with M = micro-batch * seq tokens and H the hidden size (bytes):
   reversible  one block's reconstruction context (LN outputs, packed QKV, attention output,
               GELU pre-activation and output, both reconstructed inputs) ~ 36 M H, plus the
-              gradient scratch of one block ~ 38 M H; PaReprop keeps two contexts.  Independent
-              of the pipeline depth and of the blocks per stage.
+              kernels' reusable scratch of the forward and of the VJPs and the block's fp32
+              gradients ~ 90 M H (fitted to a measured peak: 126.6 M H of activations at
+              M = 8192, H = 1024); PaReprop keeps two contexts.  Independent of the pipeline
+              depth and of the blocks per stage.
   standard    ~ 36 M H per block per in-flight micro-batch, blocks x (P - stage) in flight.
   checkpoint  the fp32 stage input per in-flight micro-batch (P - stage) plus one stage of
               recomputed contexts.
@@ -48,7 +50,7 @@ def predict_breakdown(cfg: GlobalConfig, stage_index: int, num_stages: int, kind
     if kind in ("reversible", "inverse"):
         recv = 2 * (2 * msg) * (stage_index > 0) + 2 * (4 * msg) * (stage_index < num_stages - 1)
         ctx = 36 * M * H
-        act = ctx * (2 if pareprop else 1) + 38 * M * H
+        act = ctx * (2 if pareprop else 1) + 90 * M * H
         if kind == "inverse":
             act = 36 * M * H * blocks + 38 * M * H
         if stage_index == num_stages - 1:
