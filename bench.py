@@ -266,6 +266,19 @@ def run_revpp(args):
         e2e = {"value": args.global_batch / (wall_max / 1e3), "unit": "samples/s", "ms_per_step": wall_max,
                "h2d_bytes_per_step": int(h2d_total), "d2h_bytes_per_step": 4,
                "api": "revpp.engine.Trainer.train_step"}
+    # ---- one more (untimed) step with a device timeline per rank: compute / bubble / exposed P2P
+    breakdown = None
+    if P > 1:
+        mine = tr.timed_train_step(batches[0])
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+        from revpp.parallel.schedule import pipeline_breakdown
+
+        pipe0 = sorted((r for r in allr if r["replica"] == 0), key=lambda r: r["stage"])
+        breakdown = {"replica": 0, "method": "CUDA events around every action's compute on the compute stream; "
+                     "bubble = the schedule's simulated idle time with each rank's measured mean action times",
+                     "per_stage": [{k: (round(v, 3) if isinstance(v, float) else v) for k, v in d.items()}
+                                   for d in pipeline_breakdown(pipe0, P, tr.v, nmb, args.schedule)]}
     loss_val = float(last) if last is not None else None
     tr.close()
     rec = base_record(args, world, "revpp")
@@ -273,6 +286,8 @@ def run_revpp(args):
                 "gpu_launches": int(launches_total), "peak_hbm_gib": peak, "clocks": clocks,
                 "device_status": status})
     rec["config"]["p2p"] = tr.p2p
+    if breakdown is not None:
+        rec["pipeline_breakdown"] = breakdown
     if loss_val is not None:
         rec["final_loss"] = loss_val
     # the loss lives on the last rank; rank 0 prints

@@ -281,6 +281,21 @@ class Trainer:
             return torch.stack(losses).mean()
         return None
 
+    def timed_train_step(self, batch: Optional[dict]) -> dict:
+        """``train_step`` with a device timeline of the pipeline part: this rank's step,
+        compute and idle time and its mean forward / backward action (ms), from CUDA events
+        on the compute stream (``revpp.parallel.schedule.StepTimeline``)."""
+        from .parallel.schedule import StepTimeline
+
+        self.executor.timeline = StepTimeline()
+        try:
+            self.train_step(batch)
+            out = self.executor.timeline.summary()
+        finally:
+            self.executor.timeline = None
+        out.update({"rank": self.rank, "stage": self.stage_index, "replica": self.replica})
+        return out
+
     def finish_step(self) -> None:
         """Replica gradient reduction, clipping and the optimizer update, then a check of the
         device status word."""

@@ -115,6 +115,71 @@ def dump_chrometrace(num_stages: int, n: int, path, schedule: str = "1f1b", t_f:
     return makespan
 
 
+class StepTimeline:
+    """Device timeline of one pipeline step on one rank: CUDA events on the compute stream
+    at the step's ends and around the compute of every action (recorded after the stream
+    waits for the action's input, so the gap before an action is the time its rank sat idle:
+    schedule bubble, transfer or synchronisation)."""
+
+    def __init__(self):
+        self.marks: List[tuple] = []  # (kind, start event, end event)
+        self.t0 = self.t1 = None
+        self._open = None
+
+    @staticmethod
+    def _ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def begin(self):
+        self.marks, self._open = [], None
+        self.t0 = self._ev()
+
+    def start(self):
+        self._open = self._ev()
+
+    def stop(self, kind: str):
+        if self._open is not None:
+            self.marks.append((kind, self._open, self._ev()))
+            self._open = None
+
+    def end(self):
+        self.t1 = self._ev()
+
+    def summary(self) -> dict:
+        """Step time, compute time, idle time and the mean forward / backward action (ms)."""
+        self.t1.synchronize()
+        step = self.t0.elapsed_time(self.t1)
+        per = {"F": [], "B": []}
+        for kind, a, b in self.marks:
+            per[kind].append(a.elapsed_time(b))
+        comp = sum(per["F"]) + sum(per["B"])
+        mean = lambda xs: sum(xs) / len(xs) if xs else 0.0  # noqa: E731
+        return {"step_ms": step, "compute_ms": comp, "idle_ms": max(0.0, step - comp),
+                "fwd_action_ms": mean(per["F"]), "bwd_action_ms": mean(per["B"]),
+                "n_fwd": len(per["F"]), "n_bwd": len(per["B"])}
+
+
+def pipeline_breakdown(rank_summaries: Sequence[dict], num_stages: int, chunks: int, n: int,
+                       schedule: str) -> List[dict]:
+    """Split every rank's idle time into the schedule's own bubble and the rest.  The bubble
+    is what ``simulate_virtual`` gives for this schedule with every rank's measured mean
+    action times and instant transfers; the rest of the idle time is exposed transfer and
+    synchronisation.  ``rank_summaries[r]`` is ``StepTimeline.summary()`` of pipeline rank r."""
+    tf = [s["fwd_action_ms"] for s in rank_summaries]
+    tb = [s["bwd_action_ms"] for s in rank_summaries]
+    sched = "interleaved" if chunks > 1 else schedule
+    span, busy = simulate_virtual(num_stages, chunks, n, sched, t_f=tf, t_b=tb)
+    out = []
+    for r, s in enumerate(rank_summaries):
+        bubble = span - busy[r]
+        out.append({"stage": r, "step_ms": s["step_ms"], "compute_ms": s["compute_ms"],
+                    "bubble_ms": min(bubble, s["idle_ms"]), "exposed_p2p_ms": max(0.0, s["idle_ms"] - bubble),
+                    "fwd_action_ms": s["fwd_action_ms"], "bwd_action_ms": s["bwd_action_ms"]})
+    return out
+
+
 class PipelineExecutor:
     """Runs a schedule on one rank.  Communication follows the reference's grouping
     (BERT/pipelining/schedules.py:700-852) on a single process group per pipeline:
@@ -134,6 +199,7 @@ class PipelineExecutor:
         self.schedule = schedule
         self.P = stage.num_stages
         self.s = stage.stage_index
+        self.timeline: Optional[StepTimeline] = None  # set to record one step's device timeline
 
     # ---------------------------------------------------------------- helpers
     def _rank(self) -> int:
@@ -154,13 +220,23 @@ class PipelineExecutor:
 
         before_forward(self._rank(), i)
         x = inputs[i] if meta is None else meta[2]
+        tl = self.timeline
+        if tl is not None:
+            tl.start()
         out = self.stage.forward(i, x, train)
+        if tl is not None:
+            tl.stop("F")
         if meta is not None:
             meta[0].release(meta[1])
         return out
 
     def _backward(self, i, meta):
+        tl = self.timeline
+        if tl is not None:
+            tl.start()
         g = self.stage.backward(i, None if meta is None else meta[2])
+        if tl is not None:
+            tl.stop("B")
         if meta is not None:
             meta[0].release(meta[1])
         return g
@@ -190,6 +266,8 @@ class PipelineExecutor:
         st = self.stage
         cm = self.comms
         st.clear()
+        if self.timeline is not None:
+            self.timeline.begin()
         if self.P > 1 and cm is not None:
             ops, buf = cm.labels_ops(labels, st.is_first, st.is_last)
             self._run(ops, [buf] if buf is not None else [])
@@ -204,6 +282,8 @@ class PipelineExecutor:
             self._backward_pass()
         else:
             self._one_f_one_b(inputs)
+        if self.timeline is not None:
+            self.timeline.end()
         return st.losses
 
     def _forward_pass(self, inputs, train: bool):
@@ -344,10 +424,13 @@ def simulate_virtual(num_stages: int, chunks: int, n: int, schedule: str = "inte
                      t_b: float = 3.0, t_comm: float = 0.0, events: list | None = None):
     """Timeline of a (virtual) pipeline schedule: every action of rank r starts when the rank
     is free and its input has arrived (``t_comm`` after the producer finished; transfers run
-    beside compute).  ``t_f`` / ``t_b`` are per chunk.  Returns (makespan, per-rank busy).
+    beside compute).  ``t_f`` / ``t_b`` are per chunk, one value or one per rank.  Returns
+    (makespan, per-rank busy).
     Raises if the action orders deadlock."""
     P, v = num_stages, chunks
     G = P * v
+    tf = list(t_f) if isinstance(t_f, (list, tuple)) else [t_f] * P
+    tb = list(t_b) if isinstance(t_b, (list, tuple)) else [t_b] * P
     acts = [virtual_actions(schedule, r, P, v, n) for r in range(P)]
     pos = [0] * P
     t = [0.0] * P
@@ -369,7 +452,7 @@ def simulate_virtual(num_stages: int, chunks: int, n: int, schedule: str = "inte
                         if src is None:
                             break
                         ready = src + t_comm
-                    dur = t_f
+                    dur = tf[r]
                 else:
                     if g == G - 1:
                         src = fdone.get((g, m))
@@ -379,7 +462,7 @@ def simulate_virtual(num_stages: int, chunks: int, n: int, schedule: str = "inte
                         ready = None if src is None else src + t_comm
                     if ready is None or (g, m) not in fdone:
                         break
-                    dur = t_b
+                    dur = tb[r]
                 start = max(t[r], ready)
                 t[r] = start + dur
                 busy[r] += dur
@@ -510,12 +593,16 @@ class ChannelExecutor:
         self.last = self.stages[-1]
         # compatibility with the single-chunk executor
         self.stage = self.first
+        self.timeline: Optional[StepTimeline] = None  # set to record one step's device timeline
 
     def step(self, inputs: Optional[Sequence] = None, labels: Optional[torch.Tensor] = None, train: bool = True):
         from .channels import ChannelError
 
         for st in self.stages:
             st.clear()
+        tl = self.timeline
+        if tl is not None:
+            tl.begin()
         try:
             lab_ch = self.chans.get("labels")
             if lab_ch is not None:
@@ -531,6 +618,8 @@ class ChannelExecutor:
                     self._fwd(c, m, inputs, train)
                 else:
                     self._bwd(c, m)
+            if tl is not None:
+                tl.end()
         except ChannelError:
             raise
         except BaseException:
@@ -552,7 +641,12 @@ class ChannelExecutor:
         else:
             cin = self.chans["fwd_in"]
             x = cin.recv()
+        tl = self.timeline
+        if tl is not None:
+            tl.start()
         out = st.forward(m, x, train)
+        if tl is not None:
+            tl.stop("F")
         if cin is not None:
             cin.release()
         if out is not None and not st.is_last:
@@ -571,7 +665,12 @@ class ChannelExecutor:
             def hook(x2, x1, _c=cout):
                 _c.put(2, x2)
                 _c.put(3, x1)
+        tl = self.timeline
+        if tl is not None:
+            tl.start()
         g = st.backward(m, msg, on_input=hook) if hook is not None else st.backward(m, msg)
+        if tl is not None:
+            tl.stop("B")
         if cin is not None:
             cin.release()
         if g is not None and cout is not None:

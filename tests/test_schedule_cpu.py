@@ -115,3 +115,21 @@ def test_channel_depth_is_deadlock_free_and_minimal(P, v):
     d = min_channel_depth(P, v, 32, sched)
     assert host_deadlock_free(P, v, 32, sched, d)
     assert host_deadlock_free(P, v, 32, sched, d + 1)
+
+
+def test_pipeline_breakdown_splits_idle_into_bubble_and_exposed():
+    from revpp.parallel.schedule import pipeline_breakdown
+
+    P, n, tf, tb = 4, 8, 1.0, 2.0
+    bubble = (P - 1) * (tf + tb)  # 1F1B idle time of every rank with equal stages
+    step = n * (tf + tb) + bubble
+    summ = [{"step_ms": step + 0.5, "compute_ms": n * (tf + tb), "idle_ms": bubble + 0.5, "fwd_action_ms": tf,
+             "bwd_action_ms": tb} for _ in range(P)]
+    out = pipeline_breakdown(summ, P, 1, n, "1f1b")
+    for d in out:
+        assert abs(d["bubble_ms"] - bubble) < 1e-9
+        assert abs(d["exposed_p2p_ms"] - 0.5) < 1e-9
+    # interleaving with 2 chunks per rank (per-chunk times halve) shrinks the simulated bubble
+    summ2 = [dict(s, fwd_action_ms=tf / 2, bwd_action_ms=tb / 2) for s in summ]
+    out2 = pipeline_breakdown(summ2, P, 2, n, "interleaved")
+    assert all(d2["bubble_ms"] < d["bubble_ms"] for d, d2 in zip(out, out2))
