@@ -79,39 +79,48 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t) {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-// 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 2) / 4 of
-// the tile.  (16 warps, each a column quarter, measured no faster: their 64 KB of staging
-// tiles cost an operand stage, and 18 warps cap the registers at 96 per thread.)
-constexpr int kGemmEpiWarps = 8;
-constexpr int kGemmColGroups = kGemmEpiWarps / 4;
-constexpr int kGemmThreads = 64 + kGemmEpiWarps * 32;
+// Epilogue warps EW = 8 or 16: warp w reads TMEM lane quarter (w % 4) and column group
+// (w - 2) / 4 of the tile (EW / 4 groups).  The epilogue-heavy instances (GELU, GELU
+// backward, residual) use 16 warps, four per scheduler, whose rounds are 32 columns so the
+// registers fit 576 threads; the others 8 warps with 64-column bf16 rounds.
+constexpr int kGemmEpiWarps = 8;  // default (plain epilogues)
+template <int EW>
+struct EpiGeom {
+  static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
+  static constexpr int kWarps = EW;
+  static constexpr int kColGroups = EW / 4;
+  static constexpr int kThreads = 64 + EW * 32;
+};
 
 // ------------------------------------------------------------------ epilogue
 // Each epilogue warp owns 32 TMEM lanes (= 32 output rows) and a run of columns.  A
 // tcgen05.ld gives every thread one row, so writing straight to global memory would make
 // each warp-wide access touch 32 different rows.  Instead every round goes through a
-// 4 KB per-warp staging tile (32 rows x 128 bytes, 16-byte units XOR-swizzled by row, which
-// keeps both access patterns at the 4-wavefront minimum): threads write their row, then
-// the warp moves 4 rows x 128 contiguous bytes per instruction, reading the residual /
-// pre-activation inputs with the same row-contiguous pattern.
+// 4 KB per-warp staging tile (32 rows of up to 128 bytes, 16-byte units XOR-swizzled by
+// row, which keeps both access patterns at the 4-wavefront minimum): threads write their
+// row, then the warp moves (32 / NU) rows of NU contiguous 16-byte units per instruction,
+// reading the residual / pre-activation inputs with the same row-contiguous pattern.
 constexpr uint32_t kEpiStageBytes = 32 * 128;
 
 __device__ __forceinline__ uint32_t epi_stg_off(int row, int unit) {
   return static_cast<uint32_t>(row * 128 + ((unit ^ (row & 7)) << 4));
 }
 
-template <int EPI>
+template <int EPI, int EW = 8>
 struct EpiTraits {
   static constexpr bool kBf16Stage = (EPI == kEpiBF16 || EPI == kEpiGelu || EPI == kEpiDGelu);
-  static constexpr int kCols = kBf16Stage ? 64 : 32;  // output columns per staged round
+  static constexpr int kCols = (kBf16Stage && EW == 8) ? 64 : 32;  // output columns per staged round
   static constexpr int kElemPerUnit = kBf16Stage ? 8 : 4;
+  static constexpr int kUnits = kCols / kElemPerUnit;  // 16-byte units per staged row: 4 or 8
+  static constexpr int kRowsPerInst = 32 / kUnits;       // rows one warp instruction covers
+  static constexpr int kIters = 32 / kRowsPerInst;       // warp instructions per round (= kUnits)
 };
 
-// Phase 1: this thread's row of the round into the staging tile.
-template <bool BF16>
+// Phase 1: this thread's row of the round (NU units) into the staging tile.
+template <bool BF16, int NU>
 __device__ __forceinline__ void epi_stage_row(uint8_t* stg, int lane, const float* v) {
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < NU; ++u) {
     uint4 w;
     if constexpr (BF16) {
       w = make_uint4(pack_bf16x2(v[8 * u + 0], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
@@ -124,16 +133,17 @@ __device__ __forceinline__ void epi_stage_row(uint8_t* stg, int lane, const floa
   }
 }
 
-// Phase 2 for a plain copy of the staged tile to a row-major output (bf16 or fp32).
-template <int ELEM_BYTES>
+// Phase 2 for a plain copy of the staged tile (NU units per row) to a row-major output.
+template <int ELEM_BYTES, int NU>
 __device__ __forceinline__ void epi_copy_out(const uint8_t* stg, int lane, void* out, long long ld, int row0, int col0,
                                              int M, int N) {
   constexpr int E = 16 / ELEM_BYTES;
-  const int u = lane & 7;
+  constexpr int RPI = 32 / NU;
+  const int u = lane % NU;
   const int col = col0 + u * E;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int rr = 4 * i + (lane >> 3);
+  for (int i = 0; i < NU; ++i) {
+    const int rr = RPI * i + lane / NU;
     const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
     if (row0 + rr < M && col < N)
       *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + ((static_cast<long long>(row0 + rr) * ld + col) * ELEM_BYTES)) = w;
@@ -141,9 +151,9 @@ __device__ __forceinline__ void epi_copy_out(const uint8_t* stg, int lane, void*
 }
 
 // Side input of an epilogue round (the fp32 residual of kEpiResid, the bf16 pre-activation
-// of kEpiDGelu): eight 16-byte units per lane, rows row0 + 4 i + lane / 8, read
-// row-contiguously like the stores.  Loaded one round ahead of its use, so the latency of
-// the global loads overlaps the previous round instead of stalling the warp.
+// of kEpiDGelu): kIters 16-byte units per lane, rows kRowsPerInst i + lane / kUnits, read
+// row-contiguously like the stores.  With 8 epilogue warps it is loaded one round ahead of
+// its use, so the latency of the global loads overlaps the previous round.
 template <int EPI>
 struct EpiSide {
   using T = uint4;
@@ -157,13 +167,14 @@ __device__ __forceinline__ constexpr bool epi_has_side() {
   return EPI == kEpiResid || EPI == kEpiDGelu;
 }
 
-template <int EPI>
+template <int EPI, int EW>
 __device__ __forceinline__ void epi_load_side(const GemmArgs& a, int lane, int row0, int col0,
-                                              typename EpiSide<EPI>::T (&sd)[8]) {
-  const int col = col0 + (lane & 7) * EpiTraits<EPI>::kElemPerUnit;
+                                              typename EpiSide<EPI>::T (&sd)[EpiTraits<EPI, EW>::kIters]) {
+  using T = EpiTraits<EPI, EW>;
+  const int col = col0 + (lane % T::kUnits) * T::kElemPerUnit;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int rr = 4 * i + (lane >> 3);
+  for (int i = 0; i < T::kIters; ++i) {
+    const int rr = T::kRowsPerInst * i + lane / T::kUnits;
     const bool ok = row0 + rr < a.M && col < a.N;
     if constexpr (EPI == kEpiResid) {
       sd[i] = ok ? *reinterpret_cast<const float4*>(a.resid + static_cast<long long>(row0 + rr) * a.ld_resid + col)
@@ -196,11 +207,14 @@ __device__ __forceinline__ void epi_prefetch_side_l2(const GemmArgs& a, int lane
 
 // One staged round: `r` holds kCols accumulator columns of this thread's row
 // (row0 + lane), starting at output column col0; `sd` the round's side input.
-template <int EPI>
+template <int EPI, int EW>
 __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* stg, int lane, int row0, int col0,
-                                                    const uint32_t* r, const typename EpiSide<EPI>::T (&sd)[8]) {
-  using T = EpiTraits<EPI>;
+                                                    const uint32_t* r,
+                                                    const typename EpiSide<EPI>::T (&sd)[EpiTraits<EPI, EW>::kIters]) {
+  using T = EpiTraits<EPI, EW>;
   constexpr int NC = T::kCols;
+  constexpr int NU = T::kUnits;
+  constexpr int RPI = T::kRowsPerInst;
   float v[NC];
 #pragma unroll
   for (int j = 0; j < NC; ++j) v[j] = __uint_as_float(r[j]);
@@ -218,18 +232,18 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       }
     }
   }
-  const int u = lane & 7;
+  const int u = lane % NU;
   const int col = col0 + u * T::kElemPerUnit;
   if constexpr (EPI == kEpiBF16 || EPI == kEpiF32) {
-    epi_stage_row<T::kBf16Stage>(stg, lane, v);
+    epi_stage_row<T::kBf16Stage, NU>(stg, lane, v);
     __syncwarp();
-    epi_copy_out<T::kBf16Stage ? 2 : 4>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
+    epi_copy_out<T::kBf16Stage ? 2 : 4, NU>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
   } else if constexpr (EPI == kEpiGelu) {
-    // unit by unit, so the GELU values never coexist with all 64 accumulators; the bf16
+    // unit by unit, so the GELU values never coexist with all the accumulators; the bf16
     // pre-activations stay packed for the optional aux_out copy
     uint32_t pre[NC / 2];
 #pragma unroll
-    for (int uu = 0; uu < NC / 8; ++uu) {
+    for (int uu = 0; uu < NU; ++uu) {
       uint32_t hw[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -240,26 +254,27 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, uu)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
     __syncwarp();
-    epi_copy_out<2>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
+    epi_copy_out<2, NU>(stg, lane, a.C, a.ldc, row0, col0, a.M, a.N);
     if (a.aux_out != nullptr) {
       __syncwarp();
 #pragma unroll
-      for (int uu = 0; uu < NC / 8; ++uu)
+      for (int uu = 0; uu < NU; ++uu)
         *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, uu)) =
             make_uint4(pre[4 * uu], pre[4 * uu + 1], pre[4 * uu + 2], pre[4 * uu + 3]);
       __syncwarp();
-      epi_copy_out<2>(stg, lane, a.aux_out, a.ld_aux, row0, col0, a.M, a.N);
+      epi_copy_out<2, NU>(stg, lane, a.aux_out, a.ld_aux, row0, col0, a.M, a.N);
     }
-  } else if constexpr (EPI == kEpiResid) {
+  }
+  else if constexpr (EPI == kEpiResid) {
     // C = resid + sign * bf16(acc + bias)
 #pragma unroll
     for (int j = 0; j < NC; ++j) v[j] = bf16r(v[j]);
-    epi_stage_row<false>(stg, lane, v);
+    epi_stage_row<false, NU>(stg, lane, v);
     __syncwarp();
     const float sg = a.sign;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = 4 * i + (lane >> 3);
+    for (int i = 0; i < T::kIters; ++i) {
+      const int rr = RPI * i + lane / NU;
       const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
       if (row0 + rr < a.M && col < a.N) {
         *reinterpret_cast<float4*>(static_cast<float*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col) =
@@ -270,12 +285,12 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
   } else if constexpr (EPI == kEpiDGelu) {
     // C = bf16(bf16(acc) * gelu'(aux)), aux = pre-activation; with colsum_part, the column
     // sums of this round's 32 rows go to row row0 / 32 of the partial-sum buffer
-    epi_stage_row<true>(stg, lane, v);
+    epi_stage_row<true, NU>(stg, lane, v);
     __syncwarp();
     float cs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = 4 * i + (lane >> 3);
+    for (int i = 0; i < T::kIters; ++i) {
+      const int rr = RPI * i + lane / NU;
       const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
       if (row0 + rr < a.M && col < a.N) {
         const uint32_t wa[4] = {w.x, w.y, w.z, w.w};
@@ -295,24 +310,24 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       }
     }
     if (a.colsum_part != nullptr) {  // warp-uniform
-      // lanes u, u + 8, u + 16, u + 24 hold the same 8 columns (different rows)
+      // lanes with the same lane % NU hold the same 8 columns (different rows)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 8);
-        cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], 16);
+#pragma unroll
+        for (int m = NU; m < 32; m <<= 1) cs[e] += __shfl_xor_sync(0xffffffffu, cs[e], m);
       }
-      if (lane < 8 && row0 < a.M && col < a.N) {
+      if (lane < NU && row0 < a.M && col < a.N) {
         float* dst = a.colsum_part + static_cast<long long>(row0 >> 5) * a.N + col;
         *reinterpret_cast<float4*>(dst) = make_float4(cs[0], cs[1], cs[2], cs[3]);
         *reinterpret_cast<float4*>(dst + 4) = make_float4(cs[4], cs[5], cs[6], cs[7]);
       }
     }
   } else if constexpr (EPI == kEpiAtomicF32) {
-    epi_stage_row<false>(stg, lane, v);
+    epi_stage_row<false, NU>(stg, lane, v);
     __syncwarp();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = 4 * i + (lane >> 3);
+    for (int i = 0; i < T::kIters; ++i) {
+      const int rr = RPI * i + lane / NU;
       const uint4 w = *reinterpret_cast<const uint4*>(stg + epi_stg_off(rr, u));
       if (row0 + rr < a.M && col < a.N) {
         atomicAdd(reinterpret_cast<float4*>(static_cast<float*>(a.C) + static_cast<long long>(row0 + rr) * a.ldc + col),
@@ -333,44 +348,56 @@ __device__ __forceinline__ void epi_tmem_round(uint32_t taddr, uint32_t (&r)[RC]
 
 // The epilogue of one warp for one tile: WARP_COLS accumulator columns starting at TMEM
 // address `taddr` (lane quarter and column already applied), output rows row0..row0+31,
-// output columns from col0.  Epilogues with a side input run two rounds per iteration
-// with ping-pong side buffers, each loaded a round ahead.
-template <int EPI, int WARP_COLS>
+// output columns from col0.  With 8 epilogue warps, epilogues with a side input run two
+// rounds per iteration with ping-pong side buffers, each loaded a round ahead; with 16
+// the other warps of the scheduler hide the load, which is issued at the start of its round.
+template <int EPI, int WARP_COLS, int EW>
 __device__ __forceinline__ void gemm_epilogue_warp(const GemmArgs& a, uint8_t* stg, int lane, uint32_t taddr,
                                                    int row0, int col0, int next_row0 = -1, int next_col0 = 0) {
-  constexpr int RC = EpiTraits<EPI>::kCols;
+  using T = EpiTraits<EPI, EW>;
+  constexpr int RC = T::kCols;
+  constexpr int NI = T::kIters;
   using SideT = typename EpiSide<EPI>::T;
   if constexpr (epi_has_side<EPI>()) {
     if (next_row0 >= 0) epi_prefetch_side_l2<EPI, WARP_COLS>(a, lane, next_row0, next_col0);
-    SideT s0[8], s1[8];
-    epi_load_side<EPI>(a, lane, row0, col0, s0);
+  }
+  if constexpr (epi_has_side<EPI>() && EW == 8) {
+    SideT s0[NI], s1[NI];
+    epi_load_side<EPI, EW>(a, lane, row0, col0, s0);
 #pragma unroll 1
     for (int c = 0; c < WARP_COLS; c += 2 * RC) {
       if (col0 + c >= a.N) break;  // warp-uniform
       const bool more1 = c + RC < WARP_COLS && col0 + c + RC < a.N;
-      if (more1) epi_load_side<EPI>(a, lane, row0, col0 + c + RC, s1);
+      if (more1) epi_load_side<EPI, EW>(a, lane, row0, col0 + c + RC, s1);
       uint32_t r[RC];
       epi_tmem_round<RC>(taddr + c, r);
-      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r, s0);
+      gemm_epilogue_round<EPI, EW>(a, stg, lane, row0, col0 + c, r, s0);
       if (!more1) break;
-      if (c + 2 * RC < WARP_COLS && col0 + c + 2 * RC < a.N) epi_load_side<EPI>(a, lane, row0, col0 + c + 2 * RC, s0);
+      if (c + 2 * RC < WARP_COLS && col0 + c + 2 * RC < a.N)
+        epi_load_side<EPI, EW>(a, lane, row0, col0 + c + 2 * RC, s0);
       epi_tmem_round<RC>(taddr + c + RC, r);
-      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c + RC, r, s1);
+      gemm_epilogue_round<EPI, EW>(a, stg, lane, row0, col0 + c + RC, r, s1);
     }
   } else {
-    const SideT none[8] = {};
 #pragma unroll 1
     for (int c = 0; c < WARP_COLS; c += RC) {
       if (col0 + c >= a.N) break;  // warp-uniform
+      SideT sd[NI];
+      if constexpr (epi_has_side<EPI>()) {
+        epi_load_side<EPI, EW>(a, lane, row0, col0 + c, sd);
+      } else {
+#pragma unroll
+        for (int i = 0; i < NI; ++i) sd[i] = SideT{};
+      }
       uint32_t r[RC];
       epi_tmem_round<RC>(taddr + c, r);
-      gemm_epilogue_round<EPI>(a, stg, lane, row0, col0 + c, r, none);
+      gemm_epilogue_round<EPI, EW>(a, stg, lane, row0, col0 + c, r, sd);
     }
   }
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(EpiGeom<8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
   constexpr int BM = kGemmBM, BK = kGemmBK;
@@ -387,8 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // kGemmEpiWarps x 4 KB staging tiles
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kGemmEpiWarps * kEpiStageBytes);
+  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // EpiGeom<8>::kWarps x 4 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + EpiGeom<8>::kWarps * kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -407,8 +434,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(&tfull[0], 1);
     mbar_init(&tfull[1], 1);
-    mbar_init(&tempty[0], kGemmEpiWarps);
-    mbar_init(&tempty[1], kGemmEpiWarps);
+    mbar_init(&tempty[0], EpiGeom<8>::kWarps);
+    mbar_init(&tempty[1], EpiGeom<8>::kWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -541,15 +568,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / EpiGeom<8>::kColGroups));
       int nrow = -1, ncol = 0;
       if (t + t_step < num_tiles) {
         const TileCoord nc = tile_coord(args, t + t_step);
         nrow = nc.tm * BM + q * 32;
-        ncol = nc.tn * BN + cg * (BN / kGemmColGroups);
+        ncol = nc.tn * BN + cg * (BN / EpiGeom<8>::kColGroups);
       }
-      gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tc.tm * BM + q * 32,
-                                                   tc.tn * BN + cg * (BN / kGemmColGroups), nrow, ncol);
+      gemm_epilogue_warp<EPI, BN / EpiGeom<8>::kColGroups, 8>(args, sEpi + ew * kEpiStageBytes, lane, taddr, tc.tm * BM + q * 32,
+                                                   tc.tn * BN + cg * (BN / EpiGeom<8>::kColGroups), nrow, ncol);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -580,8 +607,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //     and `drain` in both CTAs with a multicast commit;
 //   - the leader's `tempty` barrier counts the epilogue warps of both CTAs (the peer's
 //     arrive remotely), so the accumulator is reused only after both halves are read.
-template <int STAGES, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int STAGES, bool A_MN, bool B_MN, int EPI, int EW>
+__global__ void __launch_bounds__(EpiGeom<EW>::kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmArgs args) {
   constexpr int BM = 128, BN = 256, BK = kGemmBK;  // per CTA: 128 A rows, 128 B rows; tile 256 x 256
@@ -597,8 +624,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // kGemmEpiWarps x 4 KB staging tiles
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kGemmEpiWarps * kEpiStageBytes);
+  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;  // EpiGeom<EW>::kWarps x 4 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + EpiGeom<EW>::kWarps * kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -619,8 +646,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(&tfull[0], 1);
     mbar_init(&tfull[1], 1);
-    mbar_init(&tempty[0], 2 * kGemmEpiWarps);
-    mbar_init(&tempty[1], 2 * kGemmEpiWarps);
+    mbar_init(&tempty[0], 2 * EpiGeom<EW>::kWarps);
+    mbar_init(&tempty[1], 2 * EpiGeom<EW>::kWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -767,16 +794,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / kGemmColGroups));
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cg * (BN / EpiGeom<EW>::kColGroups));
       int nrow = -1, ncol = 0;
       if (t + t_step < num_tiles) {
         const TileCoord nc = tile_coord(args, t + t_step);
         nrow = nc.tm * 2 * BM + crank * BM + q * 32;
-        ncol = nc.tn * BN + cg * (BN / kGemmColGroups);
+        ncol = nc.tn * BN + cg * (BN / EpiGeom<EW>::kColGroups);
       }
-      gemm_epilogue_warp<EPI, BN / kGemmColGroups>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
+      gemm_epilogue_warp<EPI, BN / EpiGeom<EW>::kColGroups, EW>(args, sEpi + ew * kEpiStageBytes, lane, taddr,
                                                    tc.tm * 2 * BM + crank * BM + q * 32,
-                                                   tc.tn * BN + cg * (BN / kGemmColGroups), nrow, ncol);
+                                                   tc.tn * BN + cg * (BN / EpiGeom<EW>::kColGroups), nrow, ncol);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
@@ -839,15 +866,15 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     REVPP_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured_for = dev;
   }
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, args);
+  kern<<<grid, EpiGeom<8>::kThreads, smem, st>>>(ta, tb, args);
   REVPP_CHECK_LAUNCH();
 }
 
-template <int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int STAGES, bool A_MN, bool B_MN, int EPI, int EW>
 void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                        cudaStream_t st) {
-  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + 128 * kGemmBK * 2) + kGemmEpiWarps * kEpiStageBytes + 1024 + 256;
-  auto kern = gemm_tc2_kernel<STAGES, A_MN, B_MN, EPI>;
+  constexpr int smem = STAGES * (kGemmBM * kGemmBK * 2 + 128 * kGemmBK * 2) + EW * kEpiStageBytes + 1024 + 256;
+  auto kern = gemm_tc2_kernel<STAGES, A_MN, B_MN, EPI, EW>;
   static int configured_for = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -857,7 +884,7 @@ void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(EpiGeom<EW>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -873,24 +900,38 @@ void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
 
 void dispatch_gemm2(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                     const GemmArgs& args, int grid, cudaStream_t st) {
-  constexpr int ST = 6;  // 6 x 32 KB operand stages + 8 x 4 KB epilogue staging tiles
+  constexpr int ST = 6;   // 6 x 32 KB operand stages + 8 x 4 KB epilogue staging tiles
+  constexpr int ST16 = 5;  // 5 x 32 KB operand stages + 16 x 4 KB epilogue staging tiles
+  // 16 epilogue warps for the GELU epilogue and the residual epilogue of the K = 1024
+  // GEMMs (measured at M = 32768: 257 -> 245 us, 92 -> 86 us); with K = 4096 the sixth
+  // operand stage is worth more than the wider epilogue, and the GELU-backward epilogue
+  // was slower on 16 warps (284 -> 290 us).  REVPP_GEMM_EPI_WARPS=8 keeps 8 everywhere.
+  static const bool wide = [] {
+    const char* e = std::getenv("REVPP_GEMM_EPI_WARPS");
+    return e == nullptr || std::atoi(e) != 8;
+  }();
   if (!a_mn && !b_mn) {
     switch (epi) {
-      case kEpiBF16: return launch_gemm2_inst<ST, false, false, kEpiBF16>(ta, tb, args, grid, st);
-      case kEpiGelu: return launch_gemm2_inst<ST, false, false, kEpiGelu>(ta, tb, args, grid, st);
-      case kEpiResid: return launch_gemm2_inst<ST, false, false, kEpiResid>(ta, tb, args, grid, st);
-      case kEpiF32: return launch_gemm2_inst<ST, false, false, kEpiF32>(ta, tb, args, grid, st);
+      case kEpiBF16: return launch_gemm2_inst<ST, false, false, kEpiBF16, 8>(ta, tb, args, grid, st);
+      case kEpiGelu:
+        if (wide) return launch_gemm2_inst<ST16, false, false, kEpiGelu, 16>(ta, tb, args, grid, st);
+        return launch_gemm2_inst<ST, false, false, kEpiGelu, 8>(ta, tb, args, grid, st);
+      case kEpiResid:
+        if (wide && args.K <= 1024)
+          return launch_gemm2_inst<ST16, false, false, kEpiResid, 16>(ta, tb, args, grid, st);
+        return launch_gemm2_inst<ST, false, false, kEpiResid, 8>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm2_inst<ST, false, false, kEpiF32, 8>(ta, tb, args, grid, st);
       default: break;
     }
   } else if (!a_mn && b_mn) {
     switch (epi) {
-      case kEpiBF16: return launch_gemm2_inst<ST, false, true, kEpiBF16>(ta, tb, args, grid, st);
-      case kEpiDGelu: return launch_gemm2_inst<ST, false, true, kEpiDGelu>(ta, tb, args, grid, st);
-      case kEpiF32: return launch_gemm2_inst<ST, false, true, kEpiF32>(ta, tb, args, grid, st);
+      case kEpiBF16: return launch_gemm2_inst<ST, false, true, kEpiBF16, 8>(ta, tb, args, grid, st);
+      case kEpiDGelu: return launch_gemm2_inst<ST, false, true, kEpiDGelu, 8>(ta, tb, args, grid, st);
+      case kEpiF32: return launch_gemm2_inst<ST, false, true, kEpiF32, 8>(ta, tb, args, grid, st);
       default: break;
     }
   } else if (a_mn && b_mn) {
-    if (epi == kEpiAtomicF32) return launch_gemm2_inst<ST, true, true, kEpiAtomicF32>(ta, tb, args, grid, st);
+    if (epi == kEpiAtomicF32) return launch_gemm2_inst<ST, true, true, kEpiAtomicF32, 8>(ta, tb, args, grid, st);
   }
   REVPP_CHECK(false, "2-SM GEMM layout/epilogue combination not built: a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 }
