@@ -5,8 +5,10 @@
 // One CTA per (query tile of 128 rows, head, sequence); 64-key tiles.  Two softmax
 // warpgroups split the key tiles of the CTA: group w takes tiles j with j % 2 == w, with
 // its own TMEM scores S[w], output accumulator O[w], P tile, running maximum and sum, so
-// the groups never wait for each other until the end, where group 0 merges the two
-// partial results (O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / l).  Sixteen softmax warps
+// the groups never wait for each other until the end, where they exchange maxima and sums
+// and each merges half of the output columns (O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / l).
+// Optionally (REVPP_ATTN_POLY) one or two of every eight exponentials run as a polynomial
+// on the FP32 pipe (exp2_poly3) instead of the MUFU.  Sixteen softmax warps
 // per SM (two CTAs) keep the exp / max / pack work of one group running while the other
 // waits on the tensor core.
 //   warp 0     : TMA producer - Q once, then K_j / V_j into a 3-deep ring (no multicast)
@@ -40,6 +42,8 @@ constexpr uint32_t kPBytes = kQ * kKV * 2;     // 16 KB
 constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + O[2] (64 each)
 constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8
+// The kernel's template argument POLY: of every 8 probabilities of a row, this many pairs
+// are computed on the FP32 pipe (exp2_poly3) instead of the MUFU.
 constexpr uint32_t kIdescS = idesc_bf16(kQ, kKV, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16(kQ, kDh, false, true);
 
@@ -49,8 +53,8 @@ struct SmemLayout {
   static constexpr uint32_t k = q + kQBytes;                      // kStages x 8 KB
   static constexpr uint32_t v = k + kStages * kKVBytes;           // kStages x 8 KB
   static constexpr uint32_t p = v + kStages * kKVBytes;           // 2 x 16 KB (one per group)
-  static constexpr uint32_t stats = p + 2 * kPBytes;              // group 1's m, l per row
-  static constexpr uint32_t bars = stats + 2 * kQ * 4;
+  static constexpr uint32_t stats = p + 2 * kPBytes;              // m, l per row of each group
+  static constexpr uint32_t bars = stats + 4 * kQ * 4;
   static constexpr uint32_t total = bars + 256;
 };
 }  // namespace
@@ -73,6 +77,7 @@ __device__ __forceinline__ void phase_stamp(unsigned long long* ph, int k) {
   }
 }
 
+template <int POLY>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                        const AttnTcArgs args) {
@@ -90,12 +95,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* p_full = s_empty + 2;           // [2]
   uint64_t* p_empty = p_full + 2;           // [2]
   uint64_t* pv_done = p_empty + 2;          // [2] once per P V of the group (in order)
-  uint64_t* comb = pv_done + 2;             // group 1's m, l are in shared memory
-  uint64_t* drain = comb + 1;
+  uint64_t* comb = pv_done + 2;             // [2] group w's m, l are in shared memory
+  uint64_t* drain = comb + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_m1 = reinterpret_cast<float*>(smem + SmemLayout::stats);
-  float* s_l1 = s_m1 + kQ;
+  float* s_stat = reinterpret_cast<float*>(smem + SmemLayout::stats);  // [m0, l0, m1, l1][kQ]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -120,7 +124,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&p_empty[i], 1);
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(comb, 4);
+    mbar_init(&comb[0], 4);
+    mbar_init(&comb[1], 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -325,8 +330,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         float ps = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(SV(8 * c + 2 * e), sl2, -m));
-          const float p1 = ex2_approx(fmaf(SV(8 * c + 2 * e + 1), sl2, -m));
+          const float x0 = fmaf(SV(8 * c + 2 * e), sl2, -m);
+          const float x1 = fmaf(SV(8 * c + 2 * e + 1), sl2, -m);
+          const bool fma_pipe = e >= 4 - POLY;  // resolved at compile time
+          const float p0 = fma_pipe ? exp2_poly3(x0) : ex2_approx(x0);
+          const float p1 = fma_pipe ? exp2_poly3(x1) : ex2_approx(x1);
           ps += p0 + p1;
           wd[e] = pack_bf16x2(p0, p1);
         }
@@ -344,51 +352,51 @@ __global__ void __launch_bounds__(kThreads, 2)
     // this group's last P V has landed in O[w]
     bool fin = ok;
     if (fin && t > 0) fin = mbar_wait(&pv_done[w], (t - 1) & 1, args.status, abort_flag);
-    if (w == 1) {
-      // group 1 hands its maximum and sum to group 0 (m = -inf, l = 0 without key tiles)
-      s_m1[r] = fin ? m : -INFINITY;
-      s_l1[r] = fin ? l : 0.f;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(comb);
-    } else {
-      fin = fin && mbar_wait(comb, 0, args.status, abort_flag);
-      if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // merge starts
-      if (__all_sync(0xffffffffu, fin)) {
-        tc_fence_after();
-        const float m1 = s_m1[r], l1 = s_l1[r];
-        const float mx = fmaxf(m, m1);
-        const float a0 = ex2_approx(m - mx);
-        const float a1 = l1 > 0.f ? ex2_approx(m1 - mx) : 0.f;
-        const float lt = l * a0 + l1 * a1;
-        const float inv = 1.f / lt;
-        const float c0 = a0 * inv, c1 = a1 * inv;
-        const bool two = nkv >= 2;  // group 1 has key tiles (uniform over the CTA)
-        const int q = q0 + r;
-        uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh);
-#pragma unroll 1
-        for (int hh = 0; hh < 4; ++hh) {
-          uint32_t o0[16], o1[16];
-          tmem_ld16(tmem + lane_off + kTmemO + 16 * hh, o0);
-          if (two) tmem_ld16(tmem + lane_off + kTmemO + kDh + 16 * hh, o1);
-          tmem_wait_ld();
-          if (q < S) {
+    // both groups publish their maximum and sum (m = -inf, l = 0 without key tiles); then
+    // each merges and stores half of the output row: group w takes columns 32w .. 32w + 31
+    s_stat[(2 * w) * kQ + r] = fin ? m : -INFINITY;
+    s_stat[(2 * w + 1) * kQ + r] = fin ? l : 0.f;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&comb[w]);
+    fin = fin && mbar_wait(&comb[w ^ 1], 0, args.status, abort_flag);
+    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // merge starts
+    if (__all_sync(0xffffffffu, fin)) {
+      tc_fence_after();
+      const float m0 = s_stat[r], l0 = s_stat[kQ + r];
+      const float m1 = s_stat[2 * kQ + r], l1 = s_stat[3 * kQ + r];
+      const float mx = fmaxf(m0, m1);
+      const float a0 = ex2_approx(m0 - mx);  // group 0 always has key tiles: m0 is finite
+      const float a1 = l1 > 0.f ? ex2_approx(m1 - mx) : 0.f;
+      const float lt = l0 * a0 + l1 * a1;
+      const float inv = 1.f / lt;
+      const float c0 = a0 * inv, c1 = a1 * inv;
+      const bool two = nkv >= 2;  // group 1 has key tiles (uniform over the CTA)
+      const int q = q0 + r;
+      uint4* dst = reinterpret_cast<uint4*>(args.out + (static_cast<long long>(row0) + q) * H + h * kDh + 32 * w);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              float f[8];
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t col = 32 * w + 16 * hh;
+        uint32_t o0[16], o1[16];
+        tmem_ld16(tmem + lane_off + kTmemO + col, o0);
+        if (two) tmem_ld16(tmem + lane_off + kTmemO + kDh + col, o1);
+        tmem_wait_ld();
+        if (q < S) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float x1 = two ? __uint_as_float(o1[8 * c + e]) * c1 : 0.f;
-                f[e] = fmaf(__uint_as_float(o0[8 * c + e]), c0, x1);
-              }
-              dst[2 * hh + c] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                           pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+          for (int c = 0; c < 2; ++c) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float x1 = two ? __uint_as_float(o1[8 * c + e]) * c1 : 0.f;
+              f[e] = fmaf(__uint_as_float(o0[8 * c + e]), c0, x1);
             }
+            dst[2 * hh + c] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
           }
         }
-        if (q < S)
-          args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (mx + log2f(lt)) * 0.69314718055994531f;
-        if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 5);  // merge and stores issued
       }
+      if (w == 0 && q < S)
+        args.lse[(static_cast<long long>(b) * args.heads + h) * S + q] = (mx + log2f(lt)) * 0.69314718055994531f;
+      if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 5);  // merge and stores issued
     }
   }
   tc_fence_before();
@@ -428,15 +436,23 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
     a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
   }
   constexpr int smem = SmemLayout::total + 1024;
+  // REVPP_ATTN_POLY = 0..2: pairs of every 8 exponentials on the FP32 pipe (default 0)
+  static const int poly = [] {
+    const char* e = std::getenv("REVPP_ATTN_POLY");
+    const int v = e == nullptr ? 0 : std::atoi(e);
+    return v < 0 ? 0 : (v > 2 ? 2 : v);
+  }();
+  auto kern = poly == 0 ? attn_fwd_tc_kernel<0> : (poly == 1 ? attn_fwd_tc_kernel<1> : attn_fwd_tc_kernel<2>);
   static int configured_for = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_for != dev) {
-    REVPP_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    for (auto k : {attn_fwd_tc_kernel<0>, attn_fwd_tc_kernel<1>, attn_fwd_tc_kernel<2>})
+      REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured_for = dev;
   }
   dim3 grid(static_cast<unsigned>((S + kQ - 1) / kQ), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  attn_fwd_tc_kernel<<<grid, kThreads, smem, cur_stream()>>>(tq, tkv, a);
+  kern<<<grid, kThreads, smem, cur_stream()>>>(tq, tkv, a);
   REVPP_CHECK_LAUNCH();
 }
 
@@ -1209,3 +1225,24 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
     return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("launch: ") + cudaGetErrorString(e));
   return REVPP_NOALLOC_OK;
 }
+
+namespace revpp {
+// y = exp2_poly3(x) elementwise (fp32): the softmax's FP32-pipe exponential, exposed so
+// that a test can hold it to its error bound against exp2 in double precision.
+__global__ void exp2_poly3_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i < n) y[i] = exp2_poly3(x[i]);
+}
+
+void exp2_poly3_eval(const torch::Tensor& x, torch::Tensor y) {
+  check_cuda_f32(x, "x");
+  check_cuda_f32(y, "y");
+  REVPP_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel(), "x, y: same size, contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  const long long n = x.numel();
+  if (n == 0) return;
+  exp2_poly3_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cur_stream()>>>(x.data_ptr<float>(),
+                                                                                       y.data_ptr<float>(), n);
+  REVPP_CHECK_LAUNCH();
+}
+}  // namespace revpp
