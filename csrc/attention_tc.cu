@@ -7,8 +7,9 @@
 // its own TMEM scores S[w], output accumulator O[w], P tile, running maximum and sum, so
 // the groups never wait for each other until the end, where they exchange maxima and sums
 // and each merges half of the output columns (O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / l).
-// Optionally (REVPP_ATTN_POLY) one or two of every eight exponentials run as a polynomial
-// on the FP32 pipe (exp2_poly3) instead of the MUFU.  Sixteen softmax warps
+// The softmax is issue-bound, not MUFU-bound (moving a quarter of the exponentials to an
+// FP32-pipe polynomial made it slower): the scale / shift and the row sums run as packed
+// fp32 pairs (FFMA2 / FADD2) and the row maximum as three-input maxima.  Sixteen softmax warps
 // per SM (two CTAs) keep the exp / max / pack work of one group running while the other
 // waits on the tensor core.
 //   warp 0     : TMA producer - Q once, then K_j / V_j into a 3-deep ring (no multicast)
@@ -42,8 +43,8 @@ constexpr uint32_t kPBytes = kQ * kKV * 2;     // 16 KB
 constexpr uint32_t kTmemCols = 256;            // S[2] (64 each) + O[2] (64 each)
 constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 2^8
-// The kernel's template argument POLY: of every 8 probabilities of a row, this many pairs
-// are computed on the FP32 pipe (exp2_poly3) instead of the MUFU.
+// The kernel's template argument PACKED: 1 = packed fp32 pairs and three-input maxima in the
+// softmax, 0 = scalar (kept for comparison, REVPP_ATTN_PACKED=0).
 constexpr uint32_t kIdescS = idesc_bf16(kQ, kKV, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16(kQ, kDh, false, true);
 
@@ -77,7 +78,7 @@ __device__ __forceinline__ void phase_stamp(unsigned long long* ph, int k) {
   }
 }
 
-template <int POLY>
+template <int PACKED>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                        const AttnTcArgs args) {
@@ -289,10 +290,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       float pm[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) pm[i] = SV(i);
+      float tmx;
+      if constexpr (PACKED) {
 #pragma unroll
-      for (int c = 8; c < kKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], SV(c));
-      const float tmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                              fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
+        for (int c = 8; c + 16 <= kKV; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pm[i] = max3f(pm[i], SV(c + i), SV(c + 8 + i));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(pm[i], SV(kKV - 8 + i));
+        tmx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * sl2;
+      } else {
+#pragma unroll
+        for (int c = 8; c < kKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], SV(c));
+        tmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                    fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
+      }
       if (t == 0) {
         m = tmx;  // key 0 of every tile is below S, so m is finite
       } else if (__any_sync(0xffffffffu, tmx > m + kRescaleThreshold)) {
@@ -323,26 +336,45 @@ __global__ void __launch_bounds__(kThreads, 2)
         ok = false;
         break;
       }
-      float rsp[8];  // row-sum partials, one per 16-byte unit
+      if constexpr (PACKED) {
+        // x = s * scale - m and the row sums on packed pairs; four pair accumulators
+        const uint64_t sc2 = f32x2(sl2, sl2), nm2 = f32x2(-m, -m);
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // +0.0f pairs
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t wd[4];
-        float ps = 0.f;
+        for (int c = 0; c < 8; ++c) {
+          uint32_t wd[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x0 = fmaf(SV(8 * c + 2 * e), sl2, -m);
-          const float x1 = fmaf(SV(8 * c + 2 * e + 1), sl2, -m);
-          const bool fma_pipe = e >= 4 - POLY;  // resolved at compile time
-          const float p0 = fma_pipe ? exp2_poly3(x0) : ex2_approx(x0);
-          const float p1 = fma_pipe ? exp2_poly3(x1) : ex2_approx(x1);
-          ps += p0 + p1;
-          wd[e] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 4; ++e) {
+            float x0, x1;
+            f32x2_split(fma_f32x2(f32x2(SV(8 * c + 2 * e), SV(8 * c + 2 * e + 1)), sc2, nm2), x0, x1);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            acc[e] = add_f32x2(acc[e], f32x2(p0, p1));
+            wd[e] = pack_bf16x2(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
         }
-        rsp[c] = ps;
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        float a0, a1;
+        f32x2_split(add_f32x2(add_f32x2(acc[0], acc[1]), add_f32x2(acc[2], acc[3])), a0, a1);
+        l += a0 + a1;
+      } else {
+        float rsp[8];  // row-sum partials, one per 16-byte unit
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t wd[4];
+          float ps = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2_approx(fmaf(SV(8 * c + 2 * e), sl2, -m));
+            const float p1 = ex2_approx(fmaf(SV(8 * c + 2 * e + 1), sl2, -m));
+            ps += p0 + p1;
+            wd[e] = pack_bf16x2(p0, p1);
+          }
+          rsp[c] = ps;
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+        l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       }
 #undef SV
-      l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -436,18 +468,16 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
     a.phase_ns = reinterpret_cast<unsigned long long*>(phase_ns->data_ptr());
   }
   constexpr int smem = SmemLayout::total + 1024;
-  // REVPP_ATTN_POLY = 0..2: pairs of every 8 exponentials on the FP32 pipe (default 0)
-  static const int poly = [] {
-    const char* e = std::getenv("REVPP_ATTN_POLY");
-    const int v = e == nullptr ? 0 : std::atoi(e);
-    return v < 0 ? 0 : (v > 2 ? 2 : v);
+  static const bool packed = [] {
+    const char* e = std::getenv("REVPP_ATTN_PACKED");
+    return e == nullptr || std::atoi(e) != 0;
   }();
-  auto kern = poly == 0 ? attn_fwd_tc_kernel<0> : (poly == 1 ? attn_fwd_tc_kernel<1> : attn_fwd_tc_kernel<2>);
+  auto kern = packed ? attn_fwd_tc_kernel<1> : attn_fwd_tc_kernel<0>;
   static int configured_for = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_for != dev) {
-    for (auto k : {attn_fwd_tc_kernel<0>, attn_fwd_tc_kernel<1>, attn_fwd_tc_kernel<2>})
+    for (auto k : {attn_fwd_tc_kernel<0>, attn_fwd_tc_kernel<1>})
       REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured_for = dev;
   }
@@ -539,6 +569,7 @@ __device__ __forceinline__ float warp_column_sums32(float (&v)[32], int lane) {
   return v[0];
 }
 
+template <int PACKED>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
                        const AttnBwdTcArgs args) {
@@ -793,7 +824,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int q4 = 4 * k;  // first float4 of this sub-chunk's LSE / D in the warp's copy
         uint32_t pw[8], dw[8];
         bool waited = true;
-        if (key_ok) {
+        if (key_ok && PACKED) {
+          // the same on packed fp32 pairs: P = 2^(S * scale - lse), dS = bf16(P) (dP - D)
+          const uint64_t sc2 = f32x2(sl2, sl2);
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 L = s_lse4[q4 + e4];
+            const float4 Dq = s_D4[q4 + e4];
+            float x0, x1, x2, x3;
+            f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 0]), __uint_as_float(sv[4 * e4 + 1])), sc2,
+                                  f32x2(-L.x, -L.y)), x0, x1);
+            f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 2]), __uint_as_float(sv[4 * e4 + 3])), sc2,
+                                  f32x2(-L.z, -L.w)), x2, x3);
+            const uint32_t pp0 = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
+            const uint32_t pp1 = pack_bf16x2(ex2_approx(x2), ex2_approx(x3));
+            const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
+            pw[2 * e4] = pp0;
+            pw[2 * e4 + 1] = pp1;
+            const uint64_t g0 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 0]), __uint_as_float(dp[4 * e4 + 1])),
+                                          f32x2(-Dq.x, -Dq.y));
+            const uint64_t g1 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 2]), __uint_as_float(dp[4 * e4 + 3])),
+                                          f32x2(-Dq.z, -Dq.w));
+            float d0, d1, d2, d3;
+            f32x2_split(mul_f32x2(f32x2(r0.x, r0.y), g0), d0, d1);
+            f32x2_split(mul_f32x2(f32x2(r1.x, r1.y), g1), d2, d3);
+            dw[2 * e4] = pack_bf16x2(d0, d1);
+            dw[2 * e4 + 1] = pack_bf16x2(d2, d3);
+          }
+        } else if (key_ok) {
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
             const float4 L = s_lse4[q4 + e4];
@@ -969,6 +1027,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// The backward kernel instance: packed fp32-pair softmax unless REVPP_ATTN_BWD_PACKED=0.
+using AttnBwdKernel = void (*)(CUtensorMap, CUtensorMap, AttnBwdTcArgs);
+static AttnBwdKernel attn_bwd_kernel() {
+  static const bool packed = [] {
+    const char* e = std::getenv("REVPP_ATTN_BWD_PACKED");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return packed ? attn_bwd_tc_kernel<1> : attn_bwd_tc_kernel<0>;
+}
+static cudaError_t attn_bwd_set_smem(int bytes) {
+  for (AttnBwdKernel k : {attn_bwd_tc_kernel<0>, attn_bwd_tc_kernel<1>}) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 void attn_bwd_dot_launch(const torch::Tensor& dout, const torch::Tensor& out, torch::Tensor D, torch::Tensor dq_acc,
                          int64_t M, int64_t S, int64_t heads);
 void attn_dq_convert_launch(const torch::Tensor& dq_acc, torch::Tensor dqkv, int64_t M, int64_t H);
@@ -1079,11 +1154,11 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_for != dev) {
-    REVPP_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    REVPP_CUDA_CHECK(attn_bwd_set_smem(smem));
     configured_for = dev;
   }
   dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, smem, st>>>(tq, tdo, a);
+  attn_bwd_kernel()<<<grid, kBwdThreads, smem, st>>>(tq, tdo, a);
   REVPP_CHECK_LAUNCH();
   if (cs == nullptr) {
     attn_dq_convert_launch(dq_acc, dqkv, M, H);
@@ -1141,7 +1216,7 @@ cudaError_t noalloc_setup(int dev, unsigned char** scratch) {
     unsigned char* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_attn_bwd_scratch);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::total + 1024);
+    e = attn_bwd_set_smem(BwdSmem::total + 1024);
     if (e != cudaSuccess) return e;
     g_noalloc_scratch_dev[dev] = p;
   }
@@ -1213,7 +1288,7 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
   a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
   a.status = st_word;
   dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, BwdSmem::total + 1024, st>>>(tq, tdo, a);
+  attn_bwd_kernel()<<<grid, kBwdThreads, BwdSmem::total + 1024, st>>>(tq, tdo, a);
   {
     const long long n4 = M * H / 4;
     const long long threads = 256;
@@ -1225,24 +1300,3 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
     return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("launch: ") + cudaGetErrorString(e));
   return REVPP_NOALLOC_OK;
 }
-
-namespace revpp {
-// y = exp2_poly3(x) elementwise (fp32): the softmax's FP32-pipe exponential, exposed so
-// that a test can hold it to its error bound against exp2 in double precision.
-__global__ void exp2_poly3_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
-  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (i < n) y[i] = exp2_poly3(x[i]);
-}
-
-void exp2_poly3_eval(const torch::Tensor& x, torch::Tensor y) {
-  check_cuda_f32(x, "x");
-  check_cuda_f32(y, "y");
-  REVPP_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel(), "x, y: same size, contiguous");
-  c10::cuda::CUDAGuard guard(x.device());
-  const long long n = x.numel();
-  if (n == 0) return;
-  exp2_poly3_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cur_stream()>>>(x.data_ptr<float>(),
-                                                                                       y.data_ptr<float>(), n);
-  REVPP_CHECK_LAUNCH();
-}
-}  // namespace revpp

@@ -37,7 +37,6 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
                 bool zero_grad);
 void scale_(torch::Tensor x, double s);
 // attention_tc.cu
-void exp2_poly3_eval(const torch::Tensor& x, torch::Tensor y);
 void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
                  int64_t heads, const c10::optional<torch::Tensor>& phase_ns);
 void attn_fwd_persistent(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t S,
@@ -120,8 +119,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("heads"));
   m.def("attn_fwd_persistent", &revpp::attn_fwd_persistent, "persistent tcgen05 flash attention forward",
         py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"), py::arg("S"), py::arg("heads"));
-  m.def("exp2_poly3", &revpp::exp2_poly3_eval, py::arg("x"), py::arg("y"),
-        "y = 2^x by the polynomial the attention softmax runs on the FP32 pipe (tests)");
   m.def("attn_fwd_tc", &revpp::attn_fwd_tc, py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("heads"), py::arg("phase_ns") = py::none());
   m.def("attn_bwd_tc", &revpp::attn_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
