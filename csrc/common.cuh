@@ -346,22 +346,35 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FP32 and integer pipes, for the share of softmax exponentials that the
-// MUFU would otherwise queue.  Range reduction in the manner of Cody and Waite: x = n + f
-// with n = round(x), found by adding the shifter 1.5 * 2^23 (n lands in the low mantissa
-// bits), and f = x - n in [-1/2, 1/2]; 2^f from a degree-3 polynomial, a minimax fit of
-// the relative error on [-1/2, 1/2] (Lawson's iteratively reweighted least squares on
-// 2000 Chebyshev nodes, computed offline with numpy): max relative error 7.5e-5, well
-// below bf16's 2^-9; then n is added into the exponent field.  Inputs below -125 are
-// clamped there (2^-125 ~ 2e-38, zero for the bf16 probabilities and their sums; the
-// clamp keeps the result normal); inputs must stay below 128.
-__device__ __forceinline__ float exp2_poly3(float x) {
-  x = fmaxf(x, -125.f);
-  const float shifter = 12582912.f;  // 1.5 * 2^23
-  const float t = __fadd_rn(x, shifter);
-  const float f = __fsub_rn(x, __fsub_rn(t, shifter));
-  const float p = fmaf(fmaf(fmaf(0.05517166f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed pairs of fp32 (sm_100: one FFMA2 / FADD2 issue for two lanes of work) and the
+// three-input maximum.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -370,35 +383,49 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// erf(z) and exp(-z^2) together, branch-free, after Abramowitz & Stegun, Handbook of
-// Mathematical Functions (1964), formula 7.1.26:
+// erf(z) and exp(-z^2) of a pair of values, branch-free, after Abramowitz & Stegun,
+// Handbook of Mathematical Functions (1964), formula 7.1.26:
 //   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),
 // for z >= 0 with |error| <= 1.5e-7 (odd extension for z < 0).  One reciprocal and one
-// exp2 on the special-function unit, six FMAs: cheaper than a general erff in the GEMM
-// epilogues, where the GELU of every output element is computed.
-__device__ __forceinline__ float erf_and_gauss(float z, float& gauss) {
-  const float az = fabsf(z);
-  const float t = rcp_approx(fmaf(0.3275911f, az, 1.0f));
-  float poly = fmaf(1.061405429f, t, -1.453152027f);
-  poly = fmaf(poly, t, 1.421413741f);
-  poly = fmaf(poly, t, -0.284496736f);
-  poly = fmaf(poly, t, 0.254829592f);
-  poly *= t;
-  gauss = ex2_approx(-az * az * 1.4426950408889634f);  // exp(-z^2)
-  return copysignf(fmaf(-poly, gauss, 1.0f), z);
+// exp2 per value on the special-function unit; the polynomial runs on packed fp32 pairs
+// (FFMA2 / FMUL2), since the GEMM epilogues that compute the GELU of every output element
+// are issue-bound.
+__device__ __forceinline__ uint64_t f32x2_splat(float c) { return f32x2(c, c); }
+__device__ __forceinline__ void erf_and_gauss2(uint64_t z, uint64_t& e, uint64_t& gauss) {
+  float z0, z1;
+  f32x2_split(z, z0, z1);
+  const uint64_t az = f32x2(fabsf(z0), fabsf(z1));
+  float d0, d1;
+  f32x2_split(fma_f32x2(f32x2_splat(0.3275911f), az, f32x2_splat(1.0f)), d0, d1);
+  const uint64_t t = f32x2(rcp_approx(d0), rcp_approx(d1));
+  uint64_t poly = fma_f32x2(f32x2_splat(1.061405429f), t, f32x2_splat(-1.453152027f));
+  poly = fma_f32x2(poly, t, f32x2_splat(1.421413741f));
+  poly = fma_f32x2(poly, t, f32x2_splat(-0.284496736f));
+  poly = fma_f32x2(poly, t, f32x2_splat(0.254829592f));
+  poly = mul_f32x2(poly, t);
+  float q0, q1;
+  f32x2_split(mul_f32x2(mul_f32x2(az, az), f32x2_splat(-1.4426950408889634f)), q0, q1);
+  const float g0 = ex2_approx(q0), g1 = ex2_approx(q1);  // exp(-z^2)
+  gauss = f32x2(g0, g1);
+  float r0, r1;
+  f32x2_split(fma_f32x2(poly, f32x2(-g0, -g1), f32x2_splat(1.0f)), r0, r1);
+  e = f32x2(copysignf(r0, z0), copysignf(r1, z1));
 }
-
-// GELU with the exact (erf) form, x * Phi(x), and its derivative Phi(x) + x * phi(x);
-// phi(x) = exp(-x^2 / 2) / sqrt(2 pi) reuses the exponential of the erf evaluation.
-__device__ __forceinline__ float gelu_erf(float x) {
-  float g;
-  const float e = erf_and_gauss(x * 0.70710678118654752f, g);
-  return 0.5f * x * (1.0f + e);
+// GELU of the pair (x0, x1): x Phi(x) = 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ void gelu_erf2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f32x2(x0, x1);
+  uint64_t e, g;
+  erf_and_gauss2(mul_f32x2(x, f32x2_splat(0.70710678118654752f)), e, g);
+  const uint64_t hx = mul_f32x2(x, f32x2_splat(0.5f));
+  f32x2_split(fma_f32x2(e, hx, hx), y0, y1);
 }
-__device__ __forceinline__ float gelu_erf_grad(float x) {
-  float g;
-  const float e = erf_and_gauss(x * 0.70710678118654752f, g);
-  return fmaf(x * 0.39894228040143268f, g, 0.5f * (1.0f + e));
+// GELU derivative of the pair: Phi(x) + x phi(x), phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
+__device__ __forceinline__ void gelu_erf_grad2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f32x2(x0, x1);
+  uint64_t e, g;
+  erf_and_gauss2(mul_f32x2(x, f32x2_splat(0.70710678118654752f)), e, g);
+  const uint64_t phi = fma_f32x2(e, f32x2_splat(0.5f), f32x2_splat(0.5f));
+  f32x2_split(fma_f32x2(mul_f32x2(x, f32x2_splat(0.39894228040143268f)), g, phi), y0, y1);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -249,7 +249,9 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
       for (int e = 0; e < 4; ++e) {
         const float x0 = bf16r(v[8 * uu + 2 * e]), x1 = bf16r(v[8 * uu + 2 * e + 1]);
         pre[4 * uu + e] = pack_bf16x2(x0, x1);
-        hw[e] = pack_bf16x2(gelu_erf(x0), gelu_erf(x1));
+        float y0, y1;
+        gelu_erf2(x0, x1, y0, y1);
+        hw[e] = pack_bf16x2(y0, y1);
       }
       *reinterpret_cast<uint4*>(stg + epi_stg_off(lane, uu)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
@@ -300,7 +302,11 @@ __device__ __forceinline__ void gemm_epilogue_round(const GemmArgs& a, uint8_t* 
         for (int e = 0; e < 4; ++e) {
           const float2 g = unpack_bf16x2(wa[e]);
           const float2 pre = unpack_bf16x2(xa[e]);
-          o[e] = pack_bf16x2(g.x * gelu_erf_grad(pre.x), g.y * gelu_erf_grad(pre.y));
+          float d0, d1;
+          gelu_erf_grad2(pre.x, pre.y, d0, d1);
+          float o0, o1;
+          f32x2_split(mul_f32x2(f32x2(g.x, g.y), f32x2(d0, d1)), o0, o1);
+          o[e] = pack_bf16x2(o0, o1);
           const float2 rs = unpack_bf16x2(o[e]);
           cs[2 * e] += rs.x;
           cs[2 * e + 1] += rs.y;
