@@ -12,7 +12,7 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
              const c10::optional<torch::Tensor>& aux, const c10::optional<torch::Tensor>& aux_out,
              const c10::optional<torch::Tensor>& resid, double sign, int64_t splits, int64_t variant,
              const c10::optional<torch::Tensor>& colsum);
-int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K);
+int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K, int64_t sms);
 // norm.cu
 void layernorm_fwd(const torch::Tensor& x, const torch::Tensor& gamma, const torch::Tensor& beta, double eps,
                    const c10::optional<torch::Tensor>& y_bf16, const c10::optional<torch::Tensor>& y_f32,
@@ -107,7 +107,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("aux_out") = py::none(),
         py::arg("resid") = py::none(), py::arg("sign") = 1.0, py::arg("splits") = 1, py::arg("variant") = 0,
         py::arg("colsum") = py::none());
-  m.def("gemm_suggest_splits", &revpp::gemm_suggest_splits);
+  m.def("gemm_suggest_splits", &revpp::gemm_suggest_splits, py::arg("M"), py::arg("N"), py::arg("K"),
+        py::arg("sms") = -1, "split-K count for the weight-gradient GEMM (sms <= 0: this device's SM count)");
 
   m.def("layernorm_fwd", &revpp::layernorm_fwd, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps"),
         py::arg("y_bf16") = py::none(), py::arg("y_f32") = py::none(), py::arg("y2_f32") = py::none(),

@@ -39,11 +39,12 @@ def bench_gemm(a, C):
     M, N, K = a.M, a.N, a.K
     epi = EPIS[a.epi]
     dev = "cuda"
+    splits = 1
     if a.layout == "wgrad":  # C[N_out, K_in] += dY[T, N]^T X[T, K]
         A = torch.randn(K, M, device=dev).to(torch.bfloat16)
         B = torch.randn(K, N, device=dev).to(torch.bfloat16)
         out = torch.zeros(M, N, device=dev)
-        splits = C.gemm_suggest_splits(M, N, K)
+        splits = a.splits if a.splits > 0 else C.gemm_suggest_splits(M, N, K)
         fn = lambda: C.gemm_tc(A, True, B, True, M, N, K, 3, out, splits=splits, variant=a.variant)  # noqa: E731
     elif a.layout == "dgrad":
         A = torch.randn(M, K, device=dev).to(torch.bfloat16)
@@ -73,7 +74,7 @@ def bench_gemm(a, C):
     ms = _time(fn, a.warmup, a.iters)
     return {"op": "gemm" + ("-cublas" if a.cublas else ""), "layout": a.layout, "epi": a.epi, "variant": a.variant, "M": M, "N": N, "K": K,
             "colsum": bool(a.colsum), "aux_out": a.epi == "gelu" and not a.no_aux_out,
-            "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9}
+            "splits": splits if a.layout == "wgrad" else 1, "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9}
 
 
 def bench_attn(a, C, backward: bool):
@@ -224,7 +225,7 @@ def layer_suite(a):
     ]
 
 
-def main(argv=None):
+def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser()
     p.add_argument("op", choices=["gemm", "attn-fwd", "attn-bwd", "attn-phases", "layernorm", "adamw", "suite"])
     p.add_argument("--M", type=int, default=16384)
@@ -234,6 +235,7 @@ def main(argv=None):
     p.add_argument("--epi", choices=list(EPIS), default="bf16")
     p.add_argument("--layout", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     p.add_argument("--variant", type=int, default=0)
+    p.add_argument("--splits", type=int, default=0, help="wgrad: split-K count (0: the heuristic's)")
     p.add_argument("--colsum", action="store_true", help="dgelu: fused bias-gradient column sums")
     p.add_argument("--no-aux-out", action="store_true", help="gelu: do not write the pre-activation")
     p.add_argument("--B", type=int, default=16)
@@ -245,6 +247,11 @@ def main(argv=None):
     p.add_argument("--n", type=int, default=335_000_000)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=20)
+    return p
+
+
+def main(argv=None):
+    p = build_parser()
     a = p.parse_args(argv)
     from revpp.ops import ext
 
