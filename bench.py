@@ -48,8 +48,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train samples/sec + peak HBM/GPU, Rev-BERT-Large PaBER at PP=1/2/4/8 vs ref"
 MODEL = dict(hidden=1024, heads=16, layers=24, seq=512, vocab=30522, classes=2)
 # defaults of the revpp arm with several pipeline stages
-DEFAULT_P2P = "group"
-DEFAULT_SCHEDULE = "1f1b"
+DEFAULT_P2P = "copy"
+DEFAULT_SCHEDULE = "interleaved"
 
 
 def parse():

@@ -110,9 +110,9 @@ def attn_phases(a, C):
     the kernels when given a phase buffer): median time from the CTA's start to each
     phase, the median CTA duration and the kernel span.  Forward phases: 1 Q and first K
     landed, 2 first scores ready, 3 last P handed over, 4 merge starts, 5 merge done,
-    6 end.  Backward: 1 K, V, Q0, dO0 landed, 2 first S^T/dP^T ready, 3 last P^T/dS^T
-    handed over, 4 dK/dV complete, 5 dK written + column sums, 6 last dQ reduction read,
-    7 end."""
+    6 end.  Backward (persistent: phases 1-6 of the CTA's first work item): 1 K, V, Q0, dO0
+    landed, 2 first S^T/dP^T ready, 3 last P^T/dS^T handed over, 4 dK/dV complete, 5 dK
+    written + column sums, 6 its dQ reductions issued, 7 the CTA's end (all its items)."""
     B, S, heads = a.B, a.S, a.heads
     H = heads * 64
     qkv = torch.randn(B * S, 3 * H, device="cuda").to(torch.bfloat16)
@@ -139,12 +139,15 @@ def attn_phases(a, C):
             nph = 8
         torch.cuda.synchronize()
         full = ph.view(grid, 32).double()
+        full = full[full[:, 0] > 0]  # the persistent backward runs fewer CTAs than work items
         t = full[:, :nph]
         rel = (t - t[:, :1]) / 1e3  # us from the CTA's start
         res[kind] = {"phase_us_median": [round(float(x), 2) for x in rel.median(0).values],
                      "cta_us_median": round(float(rel[:, -1].median()), 2),
                      "span_us": round(float((t[:, -1].max() - t[:, 0].min()) / 1e3), 2)}
-        if kind == "bwd":  # per query tile: softmax start, hand-over, next S issued, gradient MMAs issued
+        if kind == "bwd":  # the CTA's first item; per query tile: softmax start, hand-over, next S, MMAs
+            res[kind]["first_item_us_median"] = round(float(rel[:, 5].median()), 2)
+            res[kind]["ctas"] = int(full.shape[0])
             nt = min(4, (S + 127) // 128)
             tiles = (full[:, 8:8 + 4 * nt] - full[:, :1]) / 1e3
             med = [round(float(x), 2) for x in tiles.median(0).values]

@@ -5,6 +5,7 @@ clock-event (throttle) reasons every ``period_s`` on a background thread.
 """
 from __future__ import annotations
 
+import os
 import statistics
 import threading
 import time
@@ -27,6 +28,29 @@ def decode_reasons(mask: int) -> List[str]:
     return [name for bit, name in _REASONS.items() if mask & bit]
 
 
+def _nvml_handle(pynvml, device_index: int):
+    """NVML handle of CUDA device `device_index` of this process.  NVML numbers the GPUs of
+    the machine and ignores CUDA_VISIBLE_DEVICES, so the CUDA index is mapped through the
+    device's PCI bus id (or, failing that, through CUDA_VISIBLE_DEVICES)."""
+    try:
+        import torch
+
+        pr = torch.cuda.get_device_properties(device_index)
+        bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    except Exception:  # noqa: BLE001
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if vis:
+        ent = [e.strip() for e in vis.split(",") if e.strip()]
+        if device_index < len(ent):
+            e = ent[device_index]
+            if e.isdigit():
+                return pynvml.nvmlDeviceGetHandleByIndex(int(e))
+            return pynvml.nvmlDeviceGetHandleByUUID(e)
+    return pynvml.nvmlDeviceGetHandleByIndex(device_index)
+
+
 class ClockSampler:
     def __init__(self, device_index: int = 0, period_s: float = 0.2):
         self.index = device_index
@@ -40,7 +64,7 @@ class ClockSampler:
 
             pynvml.nvmlInit()
             self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._h = _nvml_handle(pynvml, device_index)
             self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:  # noqa: BLE001
