@@ -488,8 +488,9 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 
 
 // ====================================================================== backward
-// Flash attention backward on tcgen05.  One CTA per (key tile of 128, head, sequence);
-// the CTA walks the query tiles (128 queries each):
+// Flash attention backward on tcgen05.  Persistent: one CTA per SM takes the work items
+// (key tile of 128, head, sequence) blockIdx.x, blockIdx.x + gridDim.x, ...; for each it
+// walks the query tiles (128 queries each):
 //   S^T  = K Q_j^T      (M 128 keys, N 128 queries, K 64)   -> TMEM cols [0, 128)
 //   dP^T = V dO_j^T     (same shape)                         -> TMEM cols [128, 256)
 //   softmax warps (one thread per key): P^T = exp(S^T * scale - lse_q) as bf16 pairs into
@@ -512,8 +513,13 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
 // core works on tile j.  dS^T is therefore double-buffered
 // in shared memory; P^T (one TMEM buffer) is rewritten only after the previous tile's dV
 // MMAs have read it.
+// Between items: the next item's first Q / dO tile loads while the current item ends, its K /
+// V once the current item's MMAs have completed, and its first S^T / dP^T (TMEM [0, 256))
+// runs while the dK / dV warps read the finished dK / dV out of TMEM [256, 384) and store
+// them, so set-up and write-out of an item overlap the neighbouring items' work instead of
+// leaving the SM idle (barrier and TMEM set-up happen once per CTA).
 namespace {
-constexpr int kBK = 128;  // keys per CTA
+constexpr int kBK = 128;  // keys per work item
 constexpr int kBQ = 128;  // queries per tile
 constexpr int kBwdGroups = 4;                  // softmax groups, kQG queries of a tile each
 constexpr int kQG = 128 / kBwdGroups;
@@ -529,11 +535,12 @@ struct BwdSmem {
   static constexpr uint32_t dst = dout + 2 * kTile;     // dS^T, 2 buffers
   static constexpr uint32_t stats = dst + 2 * kSqTile;  // per softmax warp: lse*log2e [kQG], D [kQG]
   static constexpr uint32_t dq = stats + 4 * kBwdGroups * 2 * kQG * 4;  // dQ_j fp32, 128 rows of 64, 272-byte stride
-  static constexpr uint32_t bars = dq + 128 * kDqStride;
+  static constexpr uint32_t red = dq + 128 * kDqStride;   // dK / dV column sums: 4 quarters x 128
+  static constexpr uint32_t bars = red + 4 * 128 * 4;
   static constexpr uint32_t total = bars + 256;
 };
 static_assert(BwdSmem::total + 1024 <= 232448, "attention backward exceeds the shared-memory limit");
-static_assert(8 * 4096 + 4 * 128 * 4 <= 2 * kSqTile, "dK/dV staging and column sums must fit in the dS^T buffers");
+static_assert(8 * 4096 <= kSqTile, "the dK / dV staging tiles must fit in one dS^T buffer");
 constexpr uint32_t kIdescSq = idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescKD = idesc_bf16(128, 64, false, true);
 constexpr uint32_t kIdescQD = idesc_bf16(128, 64, true, true);
@@ -546,7 +553,7 @@ struct AttnBwdTcArgs {
   const float* D;     // [B, heads, S]
   float* dq_acc;      // [B*S, H] fp32, zeroed
   __nv_bfloat16* dqkv;
-  int S, heads;
+  int S, heads, B;
   float scale, scale_log2;
   int* status;
   float* colsum = nullptr;  // [3H] fp32 or null: += column sums of the bf16 dK / dV written here
@@ -596,14 +603,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   float* s_stats = reinterpret_cast<float*>(smem + BwdSmem::stats);  // [softmax warp][2 kQG]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int S = args.S;
   const int H = args.heads * 64;
-  const int row0 = b * S;
-  const int k0 = kt * kBK;
   const int nq = (S + kBQ - 1) / kBQ;
-  const float* g_lse = args.lse + (static_cast<long long>(b) * args.heads + h) * S;
-  const float* g_D = args.D + (static_cast<long long>(b) * args.heads + h) * S;
+  const int nkt = (S + kBK - 1) / kBK;
+  // persistent: work item it = (key tile, head, sequence), key tile fastest; the CTA takes
+  // items blockIdx.x, blockIdx.x + gridDim.x, ...  Barrier phases follow the CTA's running
+  // counts: g = query tiles so far, n = items so far.
+  const int n_items = nkt * args.heads * args.B;
+  auto item_kt = [&](int it) { return it % nkt; };
+  auto item_h = [&](int it) { return (it / nkt) % args.heads; };
+  auto item_b = [&](int it) { return it / (nkt * args.heads); };
+  // phase stamps (measurement aid) describe the CTA's first item; slot 7 is the CTA's end
+  auto stamp = [&](int n, int slot) {
+    if (n == 0) phase_stamp(args.phase_ns, slot);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -643,23 +657,46 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      mbar_arrive_expect_tx(kv_full, 2 * kTile);
-      tma_load_2d(smem + BwdSmem::k, &tmQKV, kv_full, H + h * 64, row0 + k0);
-      tma_load_2d(smem + BwdSmem::v, &tmQKV, kv_full, 2 * H + h * 64, row0 + k0);
-      uint32_t issued = 0, issued_par = 0;
-      for (int j = 0; j < nq; ++j) {
-        const int bb = j & 1;
-        const uint32_t par = (j >> 1) & 1;
-        if (!mbar_wait(&q_empty[bb], par ^ 1u, args.status, abort_flag)) break;
-        mbar_arrive_expect_tx(&q_full[bb], 2 * kTile);
-        tma_load_2d(smem + BwdSmem::q + bb * kTile, &tmQKV, &q_full[bb], h * 64, row0 + j * kBQ);
-        tma_load_2d(smem + BwdSmem::dout + bb * kTile, &tmDO, &q_full[bb], h * 64, row0 + j * kBQ);
-        issued |= 1u << bb;
-        issued_par = (issued_par & ~(1u << bb)) | (par << bb);
+      // The query tiles of each item into the two-deep Q / dO ring; after an item's first
+      // tile (whose buffer frees a tile before the previous item ends), its K / V, once every
+      // MMA of the previous item has completed (kv_done)
+      uint32_t kv_issued = 0, issued = 0, issued_par = 0;
+      uint32_t g = 0;
+      int n = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n) {
+        const int h = item_h(it);
+        const int row0 = item_b(it) * S;
+        for (int j = 0; j < nq; ++j, ++g) {
+          const int bb = g & 1;
+          const uint32_t par = (g >> 1) & 1;
+          if (!mbar_wait(&q_empty[bb], par ^ 1u, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full[bb], 2 * kTile);
+          tma_load_2d(smem + BwdSmem::q + bb * kTile, &tmQKV, &q_full[bb], h * 64, row0 + j * kBQ);
+          tma_load_2d(smem + BwdSmem::dout + bb * kTile, &tmDO, &q_full[bb], h * 64, row0 + j * kBQ);
+          issued |= 1u << bb;
+          issued_par = (issued_par & ~(1u << bb)) | (par << bb);
+          if (j == 0) {
+            if (n > 0 && !mbar_wait(kv_done, (n - 1) & 1, args.status, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(kv_full, 2 * kTile);
+            tma_load_2d(smem + BwdSmem::k, &tmQKV, kv_full, H + h * 64, row0 + item_kt(it) * kBK);
+            tma_load_2d(smem + BwdSmem::v, &tmQKV, kv_full, 2 * H + h * 64, row0 + item_kt(it) * kBK);
+            ++kv_issued;
+          }
+        }
       }
       if (*abort_flag) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(kv_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        // let this CTA's copies in flight land before it exits
+        if (kv_issued > 0) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(kv_full, (kv_issued - 1) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+          }
         }
         for (int s = 0; s < 2; ++s) {
           if (!(issued & (1u << s))) continue;
@@ -692,71 +729,95 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         umma_commit(s_full);
       };
-      bool ok = mbar_wait(kv_full, 0, args.status, abort_flag) && mbar_wait(&q_full[0], 0, args.status, abort_flag);
-      phase_stamp(args.phase_ns, 1);  // K, V and the first Q / dO have landed
-      if (ok) {
+      uint32_t g = 0;  // query tiles so far (all of this CTA's items)
+      int n = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n) {
+        // K / V of this item; S^T / dP^T of its first tile (the softmax warps have read the
+        // previous tile's, and dK / dV of the previous item live in other TMEM columns)
+        if (!mbar_wait(kv_full, n & 1, args.status, abort_flag) ||
+            !mbar_wait(&q_full[g & 1], (g >> 1) & 1, args.status, abort_flag))
+          break;
+        stamp(n, 1);  // K, V and the first Q / dO have landed
         tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; ok && j < nq; ++j) {
-        const int bb = j & 1;
-        const uint32_t jp = j & 1;
-        const uint32_t pb = j & 1;
-        // the softmax warps have read S^T / dP^T of tile j from TMEM: start tile j+1 now,
-        // so its scores are computed while they finish tile j and its softmax overlaps
-        // this tile's gradient MMAs
-        if (!mbar_wait(s_free, jp, args.status, abort_flag)) break;
-        if (j < 4) phase_stamp(args.phase_ns, 8 + 4 * j + 2);  // tile j's scores read
-        tc_fence_after();
-        // S of tile j+1 goes first if its Q / dO rows have landed; otherwise this tile's
-        // gradient MMAs go first, so they (and the release of this tile's Q / dO buffer,
-        // which the load of tile j+2 waits for) never wait on the load of tile j+1
-        bool s_next = false;
-        if (j + 1 < nq && mbar_try_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+        issue_s(g);
+        for (int j = 0; j < nq; ++j, ++g) {
+          const int bb = g & 1;
+          const uint32_t jp = g & 1;
+          const uint32_t pb = g & 1;
+          // the softmax warps have read S^T / dP^T of tile g from TMEM: start tile g+1 now,
+          // so its scores are computed while they finish tile g and its softmax overlaps
+          // this tile's gradient MMAs
+          if (!mbar_wait(s_free, jp, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (j < 4) stamp(n, 8 + 4 * j + 2);  // tile j's scores read
           tc_fence_after();
-          issue_s(j + 1);
-          s_next = true;
-        }
-        // softmax of tile j is done: P^T of tile j is in TMEM, dS^T in buffer pb
-        if (!mbar_wait(p_full, jp, args.status, abort_flag)) break;
-        if (j < 4) phase_stamp(args.phase_ns, 8 + 4 * j + 3);  // tile j's gradient MMAs issued
-        tc_fence_after();
-        const uint32_t a_dsj = a_ds + pb * kSqTile;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          // dV += P^T dO   (A = P^T from TMEM, 16 queries = 8 columns per MMA; B = dO,
-          // MN-major: d contiguous, queries as K rows)
-          umma_bf16_ts(tmem + 256, tmem + kTmemPt + 8 * k, sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024),
-                       kIdescKD, (j > 0 || k > 0));
-        }
-        umma_commit(pt_free);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t ka = (k >> 2) * kTile + (k & 3) * 32;   // K-major over queries (2 chunks)
-          // dK += dS^T Q
-          umma_bf16_ss(tmem + 320, sdesc_sw128(a_dsj + ka, 16, 1024),
-                       sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
-        }
-        // the dQ warps have read the previous tile's dQ from TMEM (dV / dK above need not wait)
-        if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          // dQ = dS K : A = dS (queries contiguous in the dS^T tile -> MN-major, 64-query
-          // chunks 16 KB apart), B = K (MN-major: d contiguous, keys as K rows)
-          umma_bf16_ss(tmem + 384, sdesc_sw128(a_dsj + k * 2048, kTile, 1024), sdesc_sw128(a_k + k * 2048, 8192, 1024),
-                       kIdescQD, k > 0);
-        }
-        umma_commit(dq_full);
-        umma_commit(&p_empty[pb]);
-        umma_commit(&q_empty[bb]);
-        if (j + 1 < nq && !s_next) {
-          if (!mbar_wait(&q_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status, abort_flag)) break;
+          // S of tile g+1 goes first if its Q / dO rows have landed; otherwise this tile's
+          // gradient MMAs go first, so they (and the release of this tile's Q / dO buffer,
+          // which the load of tile g+2 waits for) never wait on the load of tile g+1
+          bool s_next = false;
+          if (j + 1 < nq && mbar_try_wait(&q_full[(g + 1) & 1], ((g + 1) >> 1) & 1)) {
+            tc_fence_after();
+            issue_s(g + 1);
+            s_next = true;
+          }
+          // softmax of tile g is done: P^T of tile g is in TMEM, dS^T in buffer pb.  For the
+          // item's first tile this also orders the dV / dK MMAs below (accumulate = 0) after
+          // the previous item's dK / dV were read out: the dK / dV warps drain before they
+          // take part in this tile's softmax
+          if (!mbar_wait(p_full, jp, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (j < 4) stamp(n, 8 + 4 * j + 3);  // tile j's gradient MMAs issued
           tc_fence_after();
-          issue_s(j + 1);
+          const uint32_t a_dsj = a_ds + pb * kSqTile;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            // dV += P^T dO   (A = P^T from TMEM, 16 queries = 8 columns per MMA; B = dO,
+            // MN-major: d contiguous, queries as K rows)
+            umma_bf16_ts(tmem + 256, tmem + kTmemPt + 8 * k, sdesc_sw128(a_do + bb * kTile + k * 2048, 8192, 1024),
+                         kIdescKD, (j > 0 || k > 0));
+          }
+          umma_commit(pt_free);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t ka = (k >> 2) * kTile + (k & 3) * 32;   // K-major over queries (2 chunks)
+            // dK += dS^T Q
+            umma_bf16_ss(tmem + 320, sdesc_sw128(a_dsj + ka, 16, 1024),
+                         sdesc_sw128(a_q + bb * kTile + k * 2048, 8192, 1024), kIdescKD, (j > 0 || k > 0));
+          }
+          // the dQ warps have read the previous tile's dQ from TMEM (dV / dK above need not wait)
+          if (!mbar_wait(dq_empty, jp ^ 1u, args.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            // dQ = dS K : A = dS (queries contiguous in the dS^T tile -> MN-major, 64-query
+            // chunks 16 KB apart), B = K (MN-major: d contiguous, keys as K rows)
+            umma_bf16_ss(tmem + 384, sdesc_sw128(a_dsj + k * 2048, kTile, 1024),
+                         sdesc_sw128(a_k + k * 2048, 8192, 1024), kIdescQD, k > 0);
+          }
+          umma_commit(dq_full);
+          umma_commit(&p_empty[pb]);
+          umma_commit(&q_empty[bb]);
+          if (j + 1 < nq && !s_next) {
+            if (!mbar_wait(&q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, args.status, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(g + 1);
+          }
         }
+        if (!ok) break;
+        // every MMA of this item has completed: K / V may be reloaded, dK / dV read out
+        umma_commit(kv_done);
       }
-      umma_commit(kv_done);
       umma_commit(drain);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kIntraKernelTimeoutNs) {
@@ -771,7 +832,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;      // key row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const bool key_ok = k0 + r < S;
     uint8_t* ds_base = smem + BwdSmem::dst;
     // Every softmax warp keeps its own copy of the LSE (log2 units; +inf past the sequence
     // end, so P = 0 there) and D of its group's kQG queries, fetched into registers one
@@ -779,244 +839,275 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     float* wst = s_stats + (grp * 4 + quarter) * 2 * kQG;
     const float4* s_lse4 = reinterpret_cast<const float4*>(wst);
     const float4* s_D4 = reinterpret_cast<const float4*>(wst + kQG);
-    auto fetch_stats = [&](int t, float& l2, float& dd) {
+    auto fetch_stats = [&](int it, int t, float& l2, float& dd) {
+      const long long bh = static_cast<long long>(item_b(it)) * args.heads + item_h(it);
       const int q = t * kBQ + qb + lane;
-      l2 = q < S ? g_lse[q] * 1.4426950408889634f : __int_as_float(0x7f800000);
-      dd = q < S ? g_D[q] : 0.f;
+      l2 = q < S ? args.lse[bh * S + q] * 1.4426950408889634f : __int_as_float(0x7f800000);
+      dd = q < S ? args.D[bh * S + q] : 0.f;
     };
     float nl2 = 0.f, ndd = 0.f;
-    if (nq > 0) fetch_stats(0, nl2, ndd);
+    if (static_cast<int>(blockIdx.x) < n_items) fetch_stats(blockIdx.x, 0, nl2, ndd);
     bool ok = true;
-    for (int j = 0; j < nq; ++j) {
-      const uint32_t jp = j & 1;
-      const uint32_t pb = j & 1;
-      __syncwarp();  // this warp's reads of the previous tile's stats are done
-      wst[lane] = nl2;
-      wst[kQG + lane] = ndd;
-      __syncwarp();
-      if (j + 1 < nq) fetch_stats(j + 1, nl2, ndd);
-      if (!mbar_wait(s_full, jp, args.status, abort_flag)) {
-        ok = false;
-        break;
-      }
-      if (j == 0 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 2);  // first S^T / dP^T ready
-      if (j < 4 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 8 + 4 * j + 0);  // tile j: softmax starts
-      tc_fence_after();
-      const int sw = r & 7;
-      // the dS^T tile is two 64-query swizzle chunks; this group's queries start at 16-byte
-      // unit (qb % 64) / 8 of chunk qb / 64
-      uint8_t* drow = ds_base + pb * kSqTile + (qb / 64) * kTile + (r >> 3) * 1024 + sw * 128;
-      const int u0 = (qb % 64) / 8;
-      const float sl2 = args.scale_log2;
-      // kQG / 16 sub-chunks of 16 queries (latency is hidden by the other groups' warps)
-      constexpr int KS = kQG / 16;
-#pragma unroll
-      for (int k = 0; k < KS; ++k) {
-        uint32_t sv[16], dp[16];
-        tmem_ld16(tmem + lane_off + qb + 16 * k, sv);
-        tmem_ld16(tmem + lane_off + 128 + qb + 16 * k, dp);
-        tmem_wait_ld();
-        if (k == KS - 1) {  // every S^T / dP^T column of this tile is in registers
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(s_free);
+    uint32_t g = 0;  // query tiles so far
+    int n = 0;       // items so far
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++n) {
+      const int k0 = item_kt(it) * kBK;
+      const bool key_ok = k0 + r < S;
+      for (int j = 0; j < nq; ++j, ++g) {
+        const uint32_t jp = g & 1;
+        const uint32_t pb = g & 1;
+        __syncwarp();  // this warp's reads of the previous tile's stats are done
+        wst[lane] = nl2;
+        wst[kQG + lane] = ndd;
+        __syncwarp();
+        if (j + 1 < nq) {
+          fetch_stats(it, j + 1, nl2, ndd);
+        } else if (it + static_cast<int>(gridDim.x) < n_items) {
+          fetch_stats(it + gridDim.x, 0, nl2, ndd);  // the next item's first tile
         }
-        const int q4 = 4 * k;  // first float4 of this sub-chunk's LSE / D in the warp's copy
-        uint32_t pw[8], dw[8];
-        bool waited = true;
-        if (key_ok && PACKED) {
-          // the same on packed fp32 pairs: P = 2^(S * scale - lse), dS = bf16(P) (dP - D)
-          const uint64_t sc2 = f32x2(sl2, sl2);
-#pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 L = s_lse4[q4 + e4];
-            const float4 Dq = s_D4[q4 + e4];
-            float x0, x1, x2, x3;
-            f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 0]), __uint_as_float(sv[4 * e4 + 1])), sc2,
-                                  f32x2(-L.x, -L.y)), x0, x1);
-            f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 2]), __uint_as_float(sv[4 * e4 + 3])), sc2,
-                                  f32x2(-L.z, -L.w)), x2, x3);
-            const uint32_t pp0 = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
-            const uint32_t pp1 = pack_bf16x2(ex2_approx(x2), ex2_approx(x3));
-            const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
-            pw[2 * e4] = pp0;
-            pw[2 * e4 + 1] = pp1;
-            const uint64_t g0 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 0]), __uint_as_float(dp[4 * e4 + 1])),
-                                          f32x2(-Dq.x, -Dq.y));
-            const uint64_t g1 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 2]), __uint_as_float(dp[4 * e4 + 3])),
-                                          f32x2(-Dq.z, -Dq.w));
-            float d0, d1, d2, d3;
-            f32x2_split(mul_f32x2(f32x2(r0.x, r0.y), g0), d0, d1);
-            f32x2_split(mul_f32x2(f32x2(r1.x, r1.y), g1), d2, d3);
-            dw[2 * e4] = pack_bf16x2(d0, d1);
-            dw[2 * e4 + 1] = pack_bf16x2(d2, d3);
-          }
-        } else if (key_ok) {
-#pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 L = s_lse4[q4 + e4];
-            const float4 Dq = s_D4[q4 + e4];
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 0]), sl2, -L.x));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 1]), sl2, -L.y));
-            const float p2 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 2]), sl2, -L.z));
-            const float p3 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 3]), sl2, -L.w));
-            const uint32_t pp0 = pack_bf16x2(p0, p1), pp1 = pack_bf16x2(p2, p3);
-            const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
-            pw[2 * e4] = pp0;
-            pw[2 * e4 + 1] = pp1;
-            dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[4 * e4 + 0]) - Dq.x),
-                                     r0.y * (__uint_as_float(dp[4 * e4 + 1]) - Dq.y));
-            dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[4 * e4 + 2]) - Dq.z),
-                                         r1.y * (__uint_as_float(dp[4 * e4 + 3]) - Dq.w));
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) pw[e] = dw[e] = 0u;
-        }
-        if (k == 0) {
-          // only the stores wait: the dS^T buffer must have been read by the gradient MMAs of
-          // tile j - 2, and P^T of the previous tile by its dV MMAs (warp-uniform: tcgen05.st
-          // is a warp-wide instruction); the first sub-chunk's exponentials overlap those MMAs
-          waited = mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, args.status, abort_flag);
-          if (j > 0) waited = waited && mbar_wait(pt_free, (j - 1) & 1, args.status, abort_flag);
-          waited = __all_sync(0xffffffffu, waited);
-          tc_fence_after();
-        }
-        if (!waited) {
+        if (!mbar_wait(s_full, jp, args.status, abort_flag)) {
           ok = false;
           break;
         }
-        // P^T: the 16 queries are TMEM columns kTmemPt + (qb + 16k) / 2 .. + 7 of this key's lane
-        tmem_st8(tmem + lane_off + kTmemPt + qb / 2 + 8 * k, pw);
-        // dS^T: 16 queries = 32 bytes = 16-byte units u0 + 2k, u0 + 2k + 1 of this row
+        if (j == 0 && warp == 2 && lane == 0) stamp(n, 2);  // first S^T / dP^T ready
+        if (j < 4 && warp == 2 && lane == 0) stamp(n, 8 + 4 * j + 0);  // tile j: softmax starts
+        tc_fence_after();
+        const int sw = r & 7;
+        // the dS^T tile is two 64-query swizzle chunks; this group's queries start at 16-byte
+        // unit (qb % 64) / 8 of chunk qb / 64
+        uint8_t* drow = ds_base + pb * kSqTile + (qb / 64) * kTile + (r >> 3) * 1024 + sw * 128;
+        const int u0 = (qb % 64) / 8;
+        const float sl2 = args.scale_log2;
+        // kQG / 16 sub-chunks of 16 queries (latency is hidden by the other groups' warps)
+        constexpr int KS = kQG / 16;
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const uint32_t off = ((u0 + 2 * k + t) ^ sw) << 4;
-          *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
-        }
-      }
-      if (!ok) break;
-      tmem_wait_st();
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      if (j < 4 && warp == 2 && lane == 0) phase_stamp(args.phase_ns, 8 + 4 * j + 1);  // tile j: handed over
-    }
-    // final dK (group 0) and dV (group 1) for this warp's keys; the decision is made
-    // warp-uniform since the column sums below shuffle across all lanes
-    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 3);  // last tile's P^T / dS^T handed over
-    // (groups 2 and up have no write-out)
-    bool fin = ok && grp < 2;
-    if (fin) fin = mbar_wait(kv_done, 0, args.status, abort_flag);
-    if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 4);  // dK / dV complete in TMEM
-    if (grp < 2 && __all_sync(0xffffffffu, fin)) {
-      tc_fence_after();
-      // The 64 columns of this warp's 32 key rows go through a 4 KB shared-memory tile
-      // (rows of 128 bytes, 16-byte units XOR-swizzled by row) in the dS^T buffers, which
-      // are free once kv_done has fired; the warp then stores 4 rows x 128 contiguous bytes
-      // per instruction instead of one 16-byte piece of 32 different rows.
-      uint8_t* stg = smem + BwdSmem::dst + (grp * 4 + quarter) * 4096;
-      float* red = reinterpret_cast<float*>(smem + BwdSmem::dst + 8 * 4096);  // column sums
-      // dK (TMEM cols 320..383, scaled) or dV (256..319), 32 columns per load
-#pragma unroll 1
-      for (int part = 2 * grp; part < 2 * grp + 2; ++part) {
-        const bool is_k = part < 2;
-        const int half = part & 1;
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + (is_k ? 320 : 256) + 32 * half, v);
-        tmem_wait_ld();
-        const float sc = is_k ? args.scale : 1.f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * sc, __uint_as_float(v[2 * e + 1]) * sc);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(stg + lane * 128 + (((half * 4 + u) ^ (lane & 7)) << 4)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        if (args.colsum != nullptr) {  // bias gradient of the K / V projections
-          float cv[32];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float2 r2 = unpack_bf16x2(pk[e]);
-            cv[2 * e] = key_ok ? r2.x : 0.f;
-            cv[2 * e + 1] = key_ok ? r2.y : 0.f;
+        for (int k = 0; k < KS; ++k) {
+          uint32_t sv[16], dp[16];
+          tmem_ld16(tmem + lane_off + qb + 16 * k, sv);
+          tmem_ld16(tmem + lane_off + 128 + qb + 16 * k, dp);
+          tmem_wait_ld();
+          if (k == KS - 1) {  // every S^T / dP^T column of this tile is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
           }
-          // this warp's 32 keys
-          red[quarter * 128 + part * 32 + lane] = warp_column_sums32(cv, lane);
-        }
-      }
-      __syncwarp();
-      {
-        const int u = lane & 7;
-        const long long gcol = (grp == 0 ? H : 2 * H) + h * 64 + u * 8;
+          const int q4 = 4 * k;  // first float4 of this sub-chunk's LSE / D in the warp's copy
+          uint32_t pw[8], dw[8];
+          bool waited = true;
+          if (key_ok && PACKED) {
+            // the same on packed fp32 pairs: P = 2^(S * scale - lse), dS = bf16(P) (dP - D)
+            const uint64_t sc2 = f32x2(sl2, sl2);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = 4 * i + (lane >> 3);  // key row within this warp's 32
-          const int key = k0 + quarter * 32 + rr;
-          if (key < S) {
-            *reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + key) * (3LL * H) + gcol) =
-                *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 L = s_lse4[q4 + e4];
+              const float4 Dq = s_D4[q4 + e4];
+              float x0, x1, x2, x3;
+              f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 0]), __uint_as_float(sv[4 * e4 + 1])), sc2,
+                                    f32x2(-L.x, -L.y)), x0, x1);
+              f32x2_split(fma_f32x2(f32x2(__uint_as_float(sv[4 * e4 + 2]), __uint_as_float(sv[4 * e4 + 3])), sc2,
+                                    f32x2(-L.z, -L.w)), x2, x3);
+              const uint32_t pp0 = pack_bf16x2(ex2_approx(x0), ex2_approx(x1));
+              const uint32_t pp1 = pack_bf16x2(ex2_approx(x2), ex2_approx(x3));
+              const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
+              pw[2 * e4] = pp0;
+              pw[2 * e4 + 1] = pp1;
+              const uint64_t g0 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 0]), __uint_as_float(dp[4 * e4 + 1])),
+                                            f32x2(-Dq.x, -Dq.y));
+              const uint64_t g1 = add_f32x2(f32x2(__uint_as_float(dp[4 * e4 + 2]), __uint_as_float(dp[4 * e4 + 3])),
+                                            f32x2(-Dq.z, -Dq.w));
+              float d0, d1, d2, d3;
+              f32x2_split(mul_f32x2(f32x2(r0.x, r0.y), g0), d0, d1);
+              f32x2_split(mul_f32x2(f32x2(r1.x, r1.y), g1), d2, d3);
+              dw[2 * e4] = pack_bf16x2(d0, d1);
+              dw[2 * e4 + 1] = pack_bf16x2(d2, d3);
+            }
+          } else if (key_ok) {
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 L = s_lse4[q4 + e4];
+              const float4 Dq = s_D4[q4 + e4];
+              const float p0 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 0]), sl2, -L.x));
+              const float p1 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 1]), sl2, -L.y));
+              const float p2 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 2]), sl2, -L.z));
+              const float p3 = ex2_approx(fmaf(__uint_as_float(sv[4 * e4 + 3]), sl2, -L.w));
+              const uint32_t pp0 = pack_bf16x2(p0, p1), pp1 = pack_bf16x2(p2, p3);
+              const float2 r0 = unpack_bf16x2(pp0), r1 = unpack_bf16x2(pp1);
+              pw[2 * e4] = pp0;
+              pw[2 * e4 + 1] = pp1;
+              dw[2 * e4] = pack_bf16x2(r0.x * (__uint_as_float(dp[4 * e4 + 0]) - Dq.x),
+                                       r0.y * (__uint_as_float(dp[4 * e4 + 1]) - Dq.y));
+              dw[2 * e4 + 1] = pack_bf16x2(r1.x * (__uint_as_float(dp[4 * e4 + 2]) - Dq.z),
+                                           r1.y * (__uint_as_float(dp[4 * e4 + 3]) - Dq.w));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) pw[e] = dw[e] = 0u;
+          }
+          if (k == 0) {
+            // only the stores wait: the dS^T buffer must have been read by the gradient MMAs of
+            // tile g - 2, and P^T of the previous tile by its dV MMAs (warp-uniform: tcgen05.st
+            // is a warp-wide instruction); the first sub-chunk's exponentials overlap those MMAs
+            waited = mbar_wait(&p_empty[pb], ((g >> 1) & 1) ^ 1u, args.status, abort_flag);
+            if (g > 0) waited = waited && mbar_wait(pt_free, (g - 1) & 1, args.status, abort_flag);
+            waited = __all_sync(0xffffffffu, waited);
+            tc_fence_after();
+          }
+          if (!waited) {
+            ok = false;
+            break;
+          }
+          // P^T: the 16 queries are TMEM columns kTmemPt + (qb + 16k) / 2 .. + 7 of this key's lane
+          tmem_st8(tmem + lane_off + kTmemPt + qb / 2 + 8 * k, pw);
+          // dS^T: 16 queries = 32 bytes = 16-byte units u0 + 2k, u0 + 2k + 1 of this row
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const uint32_t off = ((u0 + 2 * k + t) ^ sw) << 4;
+            *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * t], dw[4 * t + 1], dw[4 * t + 2], dw[4 * t + 3]);
           }
         }
-      }
-      if (args.colsum != nullptr) {
-        // One atomic per column and CTA: the 4 key quarters' sums are added here first (an
-        // atomic per warp put 4 x (B * S / 128) same-address atomics in L2's queue per column).
+        if (!ok) break;
+        tmem_wait_st();
+        tc_fence_before();
+        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(cs_bar);
-        if (grp == 0 && quarter == 0 && mbar_wait(cs_bar, 0, args.status, abort_flag)) {
+        if (lane == 0) mbar_arrive(p_full);
+        if (j < 4 && warp == 2 && lane == 0) stamp(n, 8 + 4 * j + 1);  // tile j: handed over
+      }
+      // final dK (group 0) and dV (group 1) for this warp's keys; the decision is made
+      // warp-uniform since the column sums below shuffle across all lanes
+      if (!ok) break;
+      if (warp == 2 && lane == 0) stamp(n, 3);  // last tile's P^T / dS^T handed over
+      // (groups 2 and up have no write-out).  The next item's first dV / dK MMAs wait for this
+      // tile's successor's softmax, which these warps run only after the read-out below.
+      if (grp < 2) {
+        const bool fin = __all_sync(0xffffffffu, mbar_wait(kv_done, n & 1, args.status, abort_flag));
+        if (warp == 2 && lane == 0) stamp(n, 4);  // dK / dV complete in TMEM
+        if (!fin) {
+          ok = false;
+          break;
+        }
+        {
+          const int h = item_h(it);
+          const int row0 = item_b(it) * S;
+          tc_fence_after();
+          // The 64 columns of this warp's 32 key rows go through a 4 KB shared-memory tile
+          // (rows of 128 bytes, 16-byte units XOR-swizzled by row) in the dS^T buffer of the
+          // item's last tile, free once kv_done has fired (the next item's first tile writes the
+          // other buffer, and its second tile only after these warps have read its first scores);
+          // the warp then stores 4 rows x 128 contiguous bytes per instruction instead of one
+          // 16-byte piece of 32 different rows.
+          uint8_t* stg = smem + BwdSmem::dst + ((g - 1) & 1) * kSqTile + (grp * 4 + quarter) * 4096;
+          float* red = reinterpret_cast<float*>(smem + BwdSmem::red);  // column sums
+          // dK (TMEM cols 320..383, scaled) or dV (256..319), 32 columns per load
+#pragma unroll 1
+          for (int part = 2 * grp; part < 2 * grp + 2; ++part) {
+            const bool is_k = part < 2;
+            const int half = part & 1;
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_off + (is_k ? 320 : 256) + 32 * half, v);
+            tmem_wait_ld();
+            const float sc = is_k ? args.scale : 1.f;
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int c = i * 32 + lane;  // 0..63 dK columns, 64..127 dV columns
-            const float sum = red[c] + red[128 + c] + red[256 + c] + red[384 + c];
-            atomicAdd(args.colsum + (c < 64 ? H : 2 * H - 64) + h * 64 + c, sum);
+            for (int e = 0; e < 16; ++e)
+              pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * sc, __uint_as_float(v[2 * e + 1]) * sc);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + (((half * 4 + u) ^ (lane & 7)) << 4)) =
+                  make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            if (args.colsum != nullptr) {  // bias gradient of the K / V projections
+              float cv[32];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const float2 r2 = unpack_bf16x2(pk[e]);
+                cv[2 * e] = key_ok ? r2.x : 0.f;
+                cv[2 * e + 1] = key_ok ? r2.y : 0.f;
+              }
+              // this warp's 32 keys
+              red[quarter * 128 + part * 32 + lane] = warp_column_sums32(cv, lane);
+            }
           }
+          __syncwarp();
+          {
+            const int u = lane & 7;
+            const long long gcol = (grp == 0 ? H : 2 * H) + h * 64 + u * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = 4 * i + (lane >> 3);  // key row within this warp's 32
+              const int key = k0 + quarter * 32 + rr;
+              if (key < S) {
+                *reinterpret_cast<uint4*>(args.dqkv + (static_cast<long long>(row0) + key) * (3LL * H) + gcol) =
+                    *reinterpret_cast<const uint4*>(stg + rr * 128 + ((u ^ (rr & 7)) << 4));
+              }
+            }
+          }
+          if (args.colsum != nullptr) {
+            // One atomic per column and CTA: the 4 key quarters' sums are added here first (an
+            // atomic per warp put 4 x (B * S / 128) same-address atomics in L2's queue per column).
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cs_bar);
+            if (grp == 0 && quarter == 0 && mbar_wait(cs_bar, n & 1, args.status, abort_flag)) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int c = i * 32 + lane;  // 0..63 dK columns, 64..127 dV columns
+                const float sum = red[c] + red[128 + c] + red[256 + c] + red[384 + c];
+                atomicAdd(args.colsum + (c < 64 ? H : 2 * H - 64) + h * 64 + c, sum);
+              }
+            }
+          }
+          if (warp == 2 && lane == 0) stamp(n, 5);  // dK written, column sums added
         }
       }
-      if (warp == 2 && lane == 0) phase_stamp(args.phase_ns, 5);  // dK written, column sums added
     }
   } else {
     // ------------------------------------------------------------------ dQ (queries)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    for (int j = 0; j < nq; ++j) {
-      if (!mbar_wait(dq_full, j & 1, args.status, abort_flag)) break;
-      tc_fence_after();
-      uint32_t dq[2][32];
-      tmem_ld32(tmem + lane_off + 384, dq[0]);
-      tmem_ld32(tmem + lane_off + 416, dq[1]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      // dQ_j * scale -> this query's 256-byte row of the staging tile, then one bulk
-      // reduction per row into the fp32 accumulator (performed in L2; per-thread vector
-      // atomics made the LSU queue and L2 the limit of this kernel's dQ path).
-      const int q = j * kBQ + r;
-      float* srow = reinterpret_cast<float*>(smem + BwdSmem::dq + r * kDqStride);
-      bulk_wait_read_all();  // the previous tile's reduction has read this row
-      const float sc = args.scale;
+    uint32_t g = 0;  // query tiles so far
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+      const int h = item_h(it);
+      const int row0 = item_b(it) * S;
+      for (int j = 0; j < nq; ++j, ++g) {
+        if (!mbar_wait(dq_full, g & 1, args.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t dq[2][32];
+        tmem_ld32(tmem + lane_off + 384, dq[0]);
+        tmem_ld32(tmem + lane_off + 416, dq[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        // dQ_j * scale -> this query's 256-byte row of the staging tile, then one bulk
+        // reduction per row into the fp32 accumulator (performed in L2; per-thread vector
+        // atomics made the LSU queue and L2 the limit of this kernel's dQ path).
+        const int q = j * kBQ + r;
+        float* srow = reinterpret_cast<float*>(smem + BwdSmem::dq + r * kDqStride);
+        bulk_wait_read_all();  // the previous tile's reduction has read this row
+        const float sc = args.scale;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        reinterpret_cast<float4*>(srow)[k] =
-            make_float4(__uint_as_float(dq[(4 * k) >> 5][(4 * k) & 31]) * sc,
-                        __uint_as_float(dq[(4 * k + 1) >> 5][(4 * k + 1) & 31]) * sc,
-                        __uint_as_float(dq[(4 * k + 2) >> 5][(4 * k + 2) & 31]) * sc,
-                        __uint_as_float(dq[(4 * k + 3) >> 5][(4 * k + 3) & 31]) * sc);
+        for (int k = 0; k < 16; ++k) {
+          reinterpret_cast<float4*>(srow)[k] =
+              make_float4(__uint_as_float(dq[(4 * k) >> 5][(4 * k) & 31]) * sc,
+                          __uint_as_float(dq[(4 * k + 1) >> 5][(4 * k + 1) & 31]) * sc,
+                          __uint_as_float(dq[(4 * k + 2) >> 5][(4 * k + 2) & 31]) * sc,
+                          __uint_as_float(dq[(4 * k + 3) >> 5][(4 * k + 3) & 31]) * sc);
+        }
+        fence_proxy_async_smem();
+        if (q < S) {
+          bulk_reduce_add_f32(args.dq_acc + (static_cast<long long>(row0) + q) * H + h * 64, srow, 256);
+          bulk_commit_group();
+        }
       }
-      fence_proxy_async_smem();
-      if (q < S) {
-        bulk_reduce_add_f32(args.dq_acc + (static_cast<long long>(row0) + q) * H + h * 64, srow, 256);
-        bulk_commit_group();
-      }
+      if (warp == 6 && lane == 0 && it == static_cast<int>(blockIdx.x)) phase_stamp(args.phase_ns, 6);
     }
     // the staging tile must outlive the reductions' reads; their writes to global memory
     // complete with the grid
     bulk_wait_read_all();
-    if (warp == 6 && lane == 0) phase_stamp(args.phase_ns, 6);  // last dQ reduction read
   }
   tc_fence_before();
   __syncthreads();
@@ -1035,6 +1126,12 @@ static AttnBwdKernel attn_bwd_kernel() {
     return e == nullptr || std::atoi(e) != 0;
   }();
   return packed ? attn_bwd_tc_kernel<1> : attn_bwd_tc_kernel<0>;
+}
+// Persistent grid: one CTA per SM (shared memory allows one) that the GEMMs also use (the
+// SMs reserved for NCCL stay free), at most one per work item.
+static unsigned attn_bwd_grid(long long B, long long S, long long heads, int sms) {
+  const long long items = ((S + kBK - 1) / kBK) * heads * B;
+  return static_cast<unsigned>(std::max<long long>(1, std::min<long long>(items, sms)));
 }
 static cudaError_t attn_bwd_set_smem(int bytes) {
   for (AttnBwdKernel k : {attn_bwd_tc_kernel<0>, attn_bwd_tc_kernel<1>}) {
@@ -1131,6 +1228,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.S = static_cast<int>(S);
   a.heads = static_cast<int>(heads);
+  a.B = static_cast<int>(B);
   a.scale = static_cast<float>(1.0 / std::sqrt(64.0));
   a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
   a.status = status_device_ptr();
@@ -1157,8 +1255,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
     REVPP_CUDA_CHECK(attn_bwd_set_smem(smem));
     configured_for = dev;
   }
-  dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  attn_bwd_kernel()<<<grid, kBwdThreads, smem, st>>>(tq, tdo, a);
+  attn_bwd_kernel()<<<attn_bwd_grid(B, S, heads, gemm_grid_sms()), kBwdThreads, smem, st>>>(tq, tdo, a);
   REVPP_CHECK_LAUNCH();
   if (cs == nullptr) {
     attn_dq_convert_launch(dq_acc, dqkv, M, H);
@@ -1255,6 +1352,10 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
   e = noalloc_setup(dev, &scratch);
   if (e != cudaSuccess)
     return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("set-up: ") + cudaGetErrorString(e));
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess)
+    return noalloc_fail(REVPP_NOALLOC_CUDA_ERROR, err, errlen, std::string("SM count: ") + cudaGetErrorString(e));
   int* st_word = status ? status : reinterpret_cast<int*>(scratch);
   float* dq_acc = reinterpret_cast<float*>(scratch + 256);
   float* Dbuf = reinterpret_cast<float*>(scratch + 256 + dq_bytes);
@@ -1284,11 +1385,12 @@ extern "C" int revpp_attn_bwd_tc_noalloc(const void* qkv, const void* out, const
   a.dqkv = static_cast<__nv_bfloat16*>(dqkv);
   a.S = S;
   a.heads = heads;
+  a.B = B;
   a.scale = static_cast<float>(1.0 / std::sqrt(64.0));
   a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(64.0));
   a.status = st_word;
-  dim3 grid(static_cast<unsigned>((S + kBK - 1) / kBK), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  attn_bwd_kernel()<<<grid, kBwdThreads, BwdSmem::total + 1024, st>>>(tq, tdo, a);
+  attn_bwd_kernel()<<<attn_bwd_grid(B, S, heads, std::max(1, sms - sm_reserve())), kBwdThreads,
+                      BwdSmem::total + 1024, st>>>(tq, tdo, a);
   {
     const long long n4 = M * H / 4;
     const long long threads = 256;
