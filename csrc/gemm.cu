@@ -1102,15 +1102,16 @@ void gemm_tc(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_m
 // Split count for the weight-gradient GEMM (K = tokens, long).  The persistent grid runs
 // 256 x 256 tiles on SM pairs; with `pt` output tiles and s splits every pair runs
 // ceil(pt s / pairs) tiles of ceil(kb / s) k-blocks, plus a fixed cost per tile (pipeline
-// fill and the atomic epilogue, about 4 k-blocks).  The split count minimising that
+// fill and the fp32 atomic epilogue, fitted as 16 k-blocks to a sweep of the four weight
+// shapes of a BERT-Large layer at 8192 and 32768 tokens).  The split count minimising that
 // makespan is taken (the smallest on ties), keeping >= 8 k-blocks per split.  At
-// N x K = 3072 x 1024 over 32768 tokens this gives 3 splits (48 tiles on 74 pairs would
-// leave a third of the machine idle with 1).  `sms` <= 0: this device's SM count.
+// N x K = 3072 x 1024 over 32768 tokens this gives 3 splits: 161 us against 223 us with 1
+// (48 tiles on 74 pairs).  `sms` <= 0: this device's SM count.
 int64_t gemm_suggest_splits(int64_t M, int64_t N, int64_t K, int64_t sms) {
   const int64_t pt = ((M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((N + 255) / 256);
   const int64_t kb = (K + kGemmBK - 1) / kGemmBK;
   const int64_t pairs = std::max<int64_t>(1, (sms > 0 ? sms : num_sms()) / 2);
-  constexpr int64_t kTileCost = 4;
+  constexpr int64_t kTileCost = 16;
   int64_t best = 1, best_cost = -1;
   for (int64_t s = 1; s <= 16; ++s) {
     if (s > 1 && kb / s < 8) break;

@@ -14,7 +14,7 @@ def _ext():
 def _makespan(M, N, K, s, sms=148):
     pt = -(-M // 256) * -(-N // 256)
     kb = -(-K // 64)
-    return -(-pt * s // (sms // 2)) * (-(-kb // s) + 4)
+    return -(-pt * s // (sms // 2)) * (-(-kb // s) + 16)
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 4096, 32768), (4096, 1024, 32768), (1024, 1024, 32768),
@@ -27,6 +27,11 @@ def test_wgrad_split_count_minimises_the_makespan(M, N, K):
     assert _makespan(M, N, K, s) == best
 
 
-def test_wgrad_split_count_fills_the_pairs_for_qkv():
-    # 48 output tiles of 3072 x 1024 on 74 SM pairs: one split would idle a third of them
-    assert _ext().gemm_suggest_splits(3072, 1024, 32768, sms=148) == 3
+def test_wgrad_split_counts_of_the_measured_sweep():
+    # the best measured split counts at 32768 / 8192 tokens (48 output tiles of 3072 x 1024
+    # on 74 SM pairs: one split would idle a third of them)
+    C = _ext()
+    assert C.gemm_suggest_splits(3072, 1024, 32768, sms=148) == 3
+    assert C.gemm_suggest_splits(1024, 4096, 32768, sms=148) == 1
+    assert C.gemm_suggest_splits(1024, 1024, 8192, sms=148) == 4
+    assert C.gemm_suggest_splits(3072, 1024, 8192, sms=148) == 3
