@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // barrier and TMEM set-up overlapped the previous kernel's tail
+  pdl_trigger();
   if (threadIdx.x == 0) phase_stamp(args.phase_ns, 0);
 
   if (warp == 0) {
@@ -482,7 +484,7 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor out, torch::Tensor lse,
     configured_for = dev;
   }
   dim3 grid(static_cast<unsigned>((S + kQ - 1) / kQ), static_cast<unsigned>(heads), static_cast<unsigned>(B));
-  kern<<<grid, kThreads, smem, cur_stream()>>>(tq, tkv, a);
+  launch_pdl(kern, grid, dim3(kThreads), smem, cur_stream(), tq, tkv, a);
   REVPP_CHECK_LAUNCH();
 }
 
@@ -652,6 +654,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // barrier and TMEM set-up overlapped the previous kernel's tail
+  pdl_trigger();
   if (threadIdx.x == 0) phase_stamp(args.phase_ns, 0);
 
   if (warp == 0) {
@@ -1255,7 +1259,8 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& out, const torch
     REVPP_CUDA_CHECK(attn_bwd_set_smem(smem));
     configured_for = dev;
   }
-  attn_bwd_kernel()<<<attn_bwd_grid(B, S, heads, gemm_grid_sms()), kBwdThreads, smem, st>>>(tq, tdo, a);
+  launch_pdl(attn_bwd_kernel(), dim3(attn_bwd_grid(B, S, heads, gemm_grid_sms())), dim3(kBwdThreads), smem, st, tq,
+             tdo, a);
   REVPP_CHECK_LAUNCH();
   if (cs == nullptr) {
     attn_dq_convert_launch(dq_acc, dqkv, M, H);

@@ -86,6 +86,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// ---------------------------------------------------------------- dependent launch
+// A kernel launched with programmatic stream serialization (launch_pdl) may start while the
+// previous kernel of its stream is finishing.  pdl_wait() returns once that kernel has
+// completed and its memory operations are visible: nothing written by earlier work may be
+// read, and nothing it reads may be written, before it.  pdl_trigger() lets the next kernel
+// of the stream launch (it then runs its own set-up and waits in pdl_wait()).  Both are
+// no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");

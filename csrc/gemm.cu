@@ -671,6 +671,8 @@ __global__ void __launch_bounds__(EpiGeom<EW>::kThreads, 1)
   cluster_sync();  // barriers of both CTAs are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();     // the set-up above overlapped the previous kernel's tail
+  pdl_trigger();
 
   const int num_tiles = args.tiles_m * args.tiles_n * args.splits;
   const int cluster_id = blockIdx.x >> 1;
@@ -893,13 +895,15 @@ void launch_gemm2_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   cfg.blockDim = dim3(EpiGeom<EW>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   REVPP_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
   count_launch();
 }

@@ -1,6 +1,8 @@
 // Host helpers: status word, device properties, TMA descriptor encoding.
 #include "host.h"
 
+#include <cstdlib>
+
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -77,6 +79,14 @@ int sm_reserve() { return g_sm_reserve; }
 int gemm_grid_sms() {
   const int n = num_sms() - g_sm_reserve;
   return n < 1 ? 1 : n;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("REVPP_PDL");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return on;
 }
 
 int num_sms() {

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 // Argument checks throw std::runtime_error (pybind11 maps it to RuntimeError).
 // c10::Error thrown through host code built by g++ here crashed the process
@@ -71,5 +72,28 @@ inline void check_cuda_f32(const torch::Tensor& t, const char* name) {
 }
 
 inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Programmatic dependent launch (on unless REVPP_PDL=0): kernels of this extension that
+// call pdl_wait() before touching memory written by earlier work of the stream (and
+// pdl_trigger() right after) are launched with the programmatic-serialization attribute,
+// so each one's launch and set-up (barriers, TMEM, descriptor prefetch) overlap the tail of
+// the kernel before it.  An operation other than a kernel in between (an event wait, a
+// copy) keeps the ordinary dependency.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  REVPP_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 
 }  // namespace revpp

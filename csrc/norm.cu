@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(kLnWarps * 32)
                   float* __restrict__ y_f32, float* __restrict__ y2_f32, long long ldy, float* __restrict__ mean_out,
                   float* __restrict__ rstd_out) {
   constexpr int H = VPL * 128;
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(kLnWarps * 32, VPL <= 8 ? 2 : 1)
                   __nv_bfloat16* __restrict__ dx_bf16, long long lddx, float* __restrict__ colsum) {
   constexpr int H = VPL * 128;
   extern __shared__ float4 s_acc4[];  // [kLnWarps][3][H / 4]
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const bool want_gb = dgamma != nullptr || dbeta != nullptr;
@@ -273,7 +277,7 @@ void layernorm_fwd(const torch::Tensor& x, const torch::Tensor& gamma, const tor
   const int grid = (M + kLnWarps - 1) / kLnWarps;
   if (M == 0) return;
   dispatch_vpl(H, [&](auto vpl) {
-    ln_fwd_kernel<decltype(vpl)::value><<<grid, kLnWarps * 32, 0, cur_stream()>>>(
+    launch_pdl(ln_fwd_kernel<decltype(vpl)::value>, dim3(grid), dim3(kLnWarps * 32), 0, cur_stream(),
         x.data_ptr<float>(), x.stride(0), gamma.data_ptr<float>(), beta.data_ptr<float>(), static_cast<float>(eps), M,
         yb, yf, yf2, ldy, opt_f32(mean), opt_f32(rstd));
   });
@@ -326,11 +330,11 @@ void layernorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch:
       configured_for[dy_bf16] = dev;
     }
     if (dy_bf16) {
-      ln_bwd_kernel<V, true><<<grid, kLnWarps * 32, smem, cur_stream()>>>(
+      launch_pdl(ln_bwd_kernel<V, true>, dim3(grid), dim3(kLnWarps * 32), smem, cur_stream(),
           dy.data_ptr(), dy.stride(0), x.data_ptr<float>(), x.stride(0), gamma.data_ptr<float>(), mean.data_ptr<float>(),
           rstd.data_ptr<float>(), M, opt_f32(dgamma), opt_f32(dbeta), rp, ldr, dxf, dxb, lddx, opt_f32(colsum));
     } else {
-      ln_bwd_kernel<V, false><<<grid, kLnWarps * 32, smem, cur_stream()>>>(
+      launch_pdl(ln_bwd_kernel<V, false>, dim3(grid), dim3(kLnWarps * 32), smem, cur_stream(),
           dy.data_ptr(), dy.stride(0), x.data_ptr<float>(), x.stride(0), gamma.data_ptr<float>(), mean.data_ptr<float>(),
           rstd.data_ptr<float>(), M, opt_f32(dgamma), opt_f32(dbeta), rp, ldr, dxf, dxb, lddx, opt_f32(colsum));
     }
