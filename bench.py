@@ -266,6 +266,16 @@ def run_revpp(args):
         e2e = {"value": args.global_batch / (wall_max / 1e3), "unit": "samples/s", "ms_per_step": wall_max,
                "h2d_bytes_per_step": int(h2d_total), "d2h_bytes_per_step": 4,
                "api": "revpp.engine.Trainer.train_step"}
+    # ---- one more (untimed) step timed on the host: how long the host takes to enqueue a step
+    # and how long the device still runs after that (a short drain means the host is the limit)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    tr.train_step(batches[0])
+    h1 = time.perf_counter()
+    torch.cuda.synchronize()
+    h2 = time.perf_counter()
+    host = {"enqueue_ms": round(max_over_ranks((h1 - h0) * 1e3, dev), 2),
+            "drain_ms_min_over_ranks": round(-max_over_ranks(-(h2 - h1) * 1e3, dev), 2)}
     # ---- one more (untimed) step with a device timeline per rank: compute / bubble / exposed P2P
     breakdown = None
     if P > 1:
@@ -286,6 +296,7 @@ def run_revpp(args):
                 "gpu_launches": int(launches_total), "peak_hbm_gib": peak, "clocks": clocks,
                 "device_status": status})
     rec["config"]["p2p"] = tr.p2p
+    rec["host"] = host
     if breakdown is not None:
         rec["pipeline_breakdown"] = breakdown
     if loss_val is not None:
