@@ -73,11 +73,16 @@ def test_vit_patch_embedding_fwd_bwd():
         assert _rel(gk[o:o + n], gt[o:o + n]) < 3e-2, name
 
 
-@pytest.mark.parametrize("model,kind,single", [("bert", "reversible", False), ("vit", "reversible", False),
-                                               ("bert", "standard", True), ("bert", "inverse", False)])
-def test_head_fwd_bwd(model, kind, single):
-    cfg, st, flat, ke, te = _stage(model, kind=kind, first=False, last=True, classes=10 if model == "vit" else 2)
-    B, S, H = 4, cfg.seq_len, 256
+# the last case has an ImageNet-sized head (1000 classes) and 20 samples: several class
+# chunks and two sample blocks in the input-gradient kernel
+@pytest.mark.parametrize("model,kind,single,classes,B", [("bert", "reversible", False, 2, 4),
+                                                         ("vit", "reversible", False, 10, 4),
+                                                         ("bert", "standard", True, 2, 4),
+                                                         ("bert", "inverse", False, 2, 4),
+                                                         ("vit", "reversible", False, 1000, 20)])
+def test_head_fwd_bwd(model, kind, single, classes, B):
+    cfg, st, flat, ke, te = _stage(model, kind=kind, first=False, last=True, classes=classes)
+    S, H = cfg.seq_len, 256
     y2 = torch.randn(B, S, H, device="cuda")
     y1 = None if single else torch.randn(B, S, H, device="cuda")
     labels = torch.randint(0, cfg.num_classes, (B,), device="cuda")
