@@ -381,11 +381,11 @@ __global__ void head_ln_fwd_kernel(const float* __restrict__ pooled, int W, cons
     hb[static_cast<long long>(b) * W + i] = __float2bfloat16_rn((x[i] - mean) * rstd * gamma[i] + beta[i]);
 }
 
-// logits[b, c] = bf16(sum_i hb[b, i] W[c, i] + bias[c]).  Block (x, y): classes 32 x .. 32 x + 31
-// (4 per warp), samples 16 y .. 16 y + 15, whose hb rows sit in shared memory (bf16).  A warp
+// logits[b, c] = bf16(sum_i hb[b, i] W[c, i] + bias[c]).  Block (x, y): classes 8 x .. 8 x + 7
+// (one per warp), samples 16 y .. 16 y + 15, whose hb rows sit in shared memory (bf16).  A warp
 // reads a class row of W once (coalesced) for its 16 samples; lane l takes elements
 // l, l + 32, ... of the row.
-constexpr int kHeadLgClasses = 32;
+constexpr int kHeadLgClasses = 8;
 constexpr int kHeadLgSamples = 16;
 __global__ void __launch_bounds__(256) head_logits_kernel(const __nv_bfloat16* __restrict__ hb,
                                                           const __nv_bfloat16* __restrict__ wb,
