@@ -179,6 +179,35 @@ __global__ void im2col_patches_kernel(const float* __restrict__ img, __nv_bfloat
   }
 }
 
+// The same for 16 x 16 patches, one patch row per thread: 16 consecutive pixels of one
+// channel (64 bytes of the image row, four float4 loads) become 16 consecutive bf16 of the
+// patch's column vector (two 16-byte stores); the index arithmetic runs once per 16
+// elements in 32-bit.  Thread t = ((b np + patch) C + c) 16 + kh.
+__global__ void im2col_patches16_kernel(const float* __restrict__ img, __nv_bfloat16* __restrict__ out, int B,
+                                        int C, int I) {
+  constexpr int p = 16;
+  const int g = I / p, np = g * g;
+  const int total = B * np * C * p;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const int kh = t % p;
+    const int c = (t / p) % C;
+    const int bp = t / (p * C);  // b np + patch
+    const int patch = bp % np, b = bp / np;
+    const int y = (patch / g) * p + kh, x0 = (patch % g) * p;
+    const float4* src = reinterpret_cast<const float4*>(img + ((static_cast<long long>(b) * C + c) * I + y) * I + x0);
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = src[q];
+      w[2 * q] = pack_bf16x2(v.x, v.y);
+      w[2 * q + 1] = pack_bf16x2(v.z, v.w);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(bp) * (C * p * p) + c * p * p + kh * p);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
 template <int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
     vit_assemble_fwd_kernel(const __nv_bfloat16* __restrict__ conv, const float* __restrict__ cls,
@@ -658,9 +687,18 @@ void im2col_patches(const torch::Tensor& img, int64_t patch, torch::Tensor out) 
   const long long n = static_cast<long long>(B) * (I / p) * (I / p) * C * p * p;
   REVPP_CHECK(out.numel() >= n, "patch buffer too small");
   c10::cuda::CUDAGuard guard(img.device());
-  im2col_patches_kernel<<<grid1d(n, 256), 256, 0, cur_stream()>>>(img.data_ptr<float>(),
-                                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B,
-                                                                    C, I, p);
+  const bool vec16 = p == 16 && I % 16 == 0 && (reinterpret_cast<uintptr_t>(img.data_ptr()) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0 &&
+                     static_cast<long long>(B) * C * I * I < (1LL << 31);
+  if (vec16) {
+    const long long rows = static_cast<long long>(B) * (I / 16) * (I / 16) * C * 16;
+    im2col_patches16_kernel<<<grid1d(rows, 256), 256, 0, cur_stream()>>>(
+        img.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B, C, I);
+  } else {
+    im2col_patches_kernel<<<grid1d(n, 256), 256, 0, cur_stream()>>>(img.data_ptr<float>(),
+                                                                      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                                                      B, C, I, p);
+  }
   REVPP_CHECK_LAUNCH();
 }
 
