@@ -86,7 +86,15 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
-// grid = S (one CTA per position), CTA loops over the batch.
+// grid = S (one CTA per position), 8 warps.  The batch rows of the position are taken 8 at a
+// time, one per warp: the warp computes its row's LayerNorm input gradient dv (the gradient
+// of the word, position and type rows), dy * x-hat and dy, adds dv to the token's word row
+// (float4 atomics in global memory: rows of different tokens), and stores the three rows in
+// shared memory; then every thread sums its columns over the 8 rows into registers (dpos,
+// dgamma, dbeta, and dtype of each row's type).  No shared-memory atomics: with every warp
+// adding into the same columns they serialised (101 us for 16 x 512 rows, 0.21 of HBM).
+// type_vocab_size <= kEmbedMaxTypes.
+constexpr int kEmbedMaxTypes = 4;
 template <int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
     bert_embed_bwd_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ tt,
@@ -96,68 +104,98 @@ __global__ void __launch_bounds__(kWarps * 32)
                           float* __restrict__ dword, float* __restrict__ dpos, float* __restrict__ dtype,
                           float* __restrict__ dgamma, float* __restrict__ dbeta) {
   constexpr int H = VPL * 128;
-  extern __shared__ float sacc[];  // [4 + T][H]: dpos, dgamma, dbeta, spare, dtype[T]
-  for (int i = threadIdx.x; i < (4 + T) * H; i += blockDim.x) sacc[i] = 0.f;
-  __syncthreads();
+  constexpr int NT = kWarps * 32;
+  constexpr int J = (H + NT - 1) / NT;  // columns per thread
+  extern __shared__ float4 sbuf4[];     // [3][kWarps][H / 4]: dv, dy * x-hat, dy of the chunk's rows
+  __shared__ int sty[kWarps];
+  float* sbuf = reinterpret_cast<float*>(sbuf4);
   const int s = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
-  for (int b = warp; b < B; b += kWarps) {
-    const long long row = static_cast<long long>(b) * S + s;
-    long long id = ids[row], ty = tt[row];
-    id = id < 0 || id >= V ? 0 : id;
-    ty = ty < 0 || ty >= T ? 0 : ty;
-    const float4* w4 = reinterpret_cast<const float4*>(word + id * H);
-    const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
-    const float4* t4 = reinterpret_cast<const float4*>(type + ty * H);
-    float4 v[VPL], dy[VPL];
+  float apos[J], ag[J], ab[J], at[kEmbedMaxTypes][J];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = lane + 32 * i;
-      v[i] = f4add(f4add(__ldg(w4 + c), __ldg(p4 + c)), __ldg(t4 + c));
-      dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
-      if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
+  for (int j = 0; j < J; ++j) {
+    apos[j] = ag[j] = ab[j] = 0.f;
+#pragma unroll
+    for (int t = 0; t < kEmbedMaxTypes; ++t) at[t][j] = 0.f;
+  }
+  for (int b0 = 0; b0 < B; b0 += kWarps) {
+    const int b = b0 + warp;
+    if (b < B) {
+      const long long row = static_cast<long long>(b) * S + s;
+      long long id = ids[row], ty = tt[row];
+      id = id < 0 || id >= V ? 0 : id;
+      ty = ty < 0 || ty >= T ? 0 : ty;
+      const float4* w4 = reinterpret_cast<const float4*>(word + id * H);
+      const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
+      const float4* t4 = reinterpret_cast<const float4*>(type + ty * H);
+      float4 v[VPL], dy[VPL];
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = f4add(f4add(__ldg(w4 + c), __ldg(p4 + c)), __ldg(t4 + c));
+        dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
+        if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
+      }
+      float mean, rstd;
+      row_stats<VPL>(v, mean, rstd, eps);
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const float4 g = __ldg(g4 + lane + 32 * i);
+        v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd,
+                           (v[i].w - mean) * rstd);
+        s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
+        s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
+      }
+      const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
+      float4* wrow = reinterpret_cast<float4*>(dword + id * H);
+      float4* r_dv = sbuf4 + (0 * kWarps + warp) * (H / 4);
+      float4* r_dx = sbuf4 + (1 * kWarps + warp) * (H / 4);
+      float4* r_dy = sbuf4 + (2 * kWarps + warp) * (H / 4);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c4 = lane + 32 * i;
+        const float4 g = __ldg(g4 + c4);
+        const float4 dv = make_float4(rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
+                                      rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2));
+        if (id != 0) atomicAdd(wrow + c4, dv);
+        r_dv[c4] = dv;
+        r_dx[c4] = make_float4(dy[i].x * v[i].x, dy[i].y * v[i].y, dy[i].z * v[i].z, dy[i].w * v[i].w);
+        r_dy[c4] = dy[i];
+      }
+      if (lane == 0) sty[warp] = static_cast<int>(ty);
     }
-    float mean, rstd;
-    row_stats<VPL>(v, mean, rstd, eps);
-    float s1 = 0.f, s2 = 0.f;
+    __syncthreads();
+    const int nr = min(kWarps, B - b0);
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const float4 g = __ldg(g4 + lane + 32 * i);
-      v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
-      s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
-      s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
-    }
-    const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
-    float* wrow = dword + id * H;
-    float* trow = sacc + (4 + ty) * H;
+    for (int j = 0; j < J; ++j) {
+      const int c = threadIdx.x + NT * j;
+      if (c < H) {
+        for (int r = 0; r < nr; ++r) {
+          const float d = sbuf[(0 * kWarps + r) * H + c];
+          apos[j] += d;
+          ag[j] += sbuf[(1 * kWarps + r) * H + c];
+          ab[j] += sbuf[(2 * kWarps + r) * H + c];
+          const int ty = sty[r];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = 4 * (lane + 32 * i);
-      const float4 g = __ldg(g4 + lane + 32 * i);
-      const float dv[4] = {rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
-                           rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2)};
-      const float dyv[4] = {dy[i].x, dy[i].y, dy[i].z, dy[i].w};
-      const float xh[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-      if (id != 0) atomicAdd(reinterpret_cast<float4*>(wrow + c), make_float4(dv[0], dv[1], dv[2], dv[3]));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        atomicAdd(&sacc[0 * H + c + j], dv[j]);
-        atomicAdd(&sacc[1 * H + c + j], dyv[j] * xh[j]);
-        atomicAdd(&sacc[2 * H + c + j], dyv[j]);
-        atomicAdd(&trow[c + j], dv[j]);
+          for (int t = 0; t < kEmbedMaxTypes; ++t)
+            if (ty == t) at[t][j] += d;
+        }
       }
     }
+    __syncthreads();  // the buffers are rewritten by the next chunk
   }
-  __syncthreads();
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    dpos[static_cast<long long>(s) * H + c] += sacc[c];  // this CTA owns row s
-    atomicAdd(dgamma + c, sacc[H + c]);
-    atomicAdd(dbeta + c, sacc[2 * H + c]);
-    for (int t = 0; t < T; ++t) {
-      const float v = sacc[(4 + t) * H + c];
-      if (v != 0.f) atomicAdd(dtype + static_cast<long long>(t) * H + c, v);
-    }
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = threadIdx.x + NT * j;
+    if (c >= H) continue;
+    dpos[static_cast<long long>(s) * H + c] += apos[j];  // this CTA owns row s
+    atomicAdd(dgamma + c, ag[j]);
+    atomicAdd(dbeta + c, ab[j]);
+#pragma unroll
+    for (int t = 0; t < kEmbedMaxTypes; ++t)
+      if (t < T && at[t][j] != 0.f) atomicAdd(dtype + static_cast<long long>(t) * H + c, at[t][j]);
   }
 }
 
@@ -248,6 +286,9 @@ __global__ void __launch_bounds__(kWarps * 32)
 }
 
 // grid = S (one CTA per token position), loops over the batch.
+// grid = S (one CTA per token position), 8 warps; the batch rows of the position are taken 8
+// at a time, one per warp, as in bert_embed_bwd_kernel: per-row gradients go to shared
+// memory, each thread sums its columns over the rows in registers (no shared-memory atomics).
 template <int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
     vit_assemble_bwd_kernel(const __nv_bfloat16* __restrict__ conv, const float* __restrict__ cls,
@@ -256,68 +297,91 @@ __global__ void __launch_bounds__(kWarps * 32)
                             __nv_bfloat16* __restrict__ dconv, float* __restrict__ dcls, float* __restrict__ dpos,
                             float* __restrict__ dgamma, float* __restrict__ dbeta) {
   constexpr int H = VPL * 128;
-  extern __shared__ float sacc[];  // [3][H]: dpos, dgamma, dbeta
-  for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) sacc[i] = 0.f;
-  __syncthreads();
+  constexpr int NT = kWarps * 32;
+  constexpr int J = (H + NT - 1) / NT;
+  extern __shared__ float4 sbuf4[];  // [3][kWarps][H / 4]: dv, dy * x-hat, dy
+  float* sbuf = reinterpret_cast<float*>(sbuf4);
   const int s = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const float4* p4 = reinterpret_cast<const float4*>(pos + static_cast<long long>(s) * H);
-  for (int b = warp; b < B; b += kWarps) {
-    const long long row = static_cast<long long>(b) * S + s;
-    float4 v[VPL], dy[VPL];
+  float apos[J], ag[J], ab[J];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = lane + 32 * i;
-      float4 a;
-      if (s == 0) {
-        a = __ldg(reinterpret_cast<const float4*>(cls) + c);
-      } else {
-        const uint2 q = *reinterpret_cast<const uint2*>(conv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + 4 * c);
-        const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
-        a = make_float4(lo.x, lo.y, hi.x, hi.y);
+  for (int j = 0; j < J; ++j) apos[j] = ag[j] = ab[j] = 0.f;
+  for (int b0 = 0; b0 < B; b0 += kWarps) {
+    const int b = b0 + warp;
+    if (b < B) {
+      const long long row = static_cast<long long>(b) * S + s;
+      float4 v[VPL], dy[VPL];
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        float4 a;
+        if (s == 0) {
+          a = __ldg(reinterpret_cast<const float4*>(cls) + c);
+        } else {
+          const uint2 q =
+              *reinterpret_cast<const uint2*>(conv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + 4 * c);
+          const float2 lo = unpack_bf16x2(q.x), hi = unpack_bf16x2(q.y);
+          a = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+        v[i] = f4add(a, __ldg(p4 + c));
+        dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
+        if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
       }
-      v[i] = f4add(a, __ldg(p4 + c));
-      dy[i] = reinterpret_cast<const float4*>(dx2 + row * H)[c];
-      if (dx1) dy[i] = f4add(dy[i], reinterpret_cast<const float4*>(dx1 + row * H)[c]);
-    }
-    float mean, rstd;
-    row_stats<VPL>(v, mean, rstd, eps);
-    float s1 = 0.f, s2 = 0.f;
+      float mean, rstd;
+      row_stats<VPL>(v, mean, rstd, eps);
+      float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const float4 g = __ldg(g4 + lane + 32 * i);
-      v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
-      s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
-      s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
-    }
-    const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = 4 * (lane + 32 * i);
-      const float4 g = __ldg(g4 + lane + 32 * i);
-      const float dv[4] = {rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
-                           rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2)};
-      const float dyv[4] = {dy[i].x, dy[i].y, dy[i].z, dy[i].w};
-      const float xh[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-      if (s > 0) {
-        *reinterpret_cast<uint2*>(dconv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + c) =
-            make_uint2(pack_bf16x2(dv[0], dv[1]), pack_bf16x2(dv[2], dv[3]));
+      for (int i = 0; i < VPL; ++i) {
+        const float4 g = __ldg(g4 + lane + 32 * i);
+        v[i] = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd,
+                           (v[i].w - mean) * rstd);
+        s1 += dy[i].x * g.x + dy[i].y * g.y + dy[i].z * g.z + dy[i].w * g.w;
+        s2 += dy[i].x * g.x * v[i].x + dy[i].y * g.y * v[i].y + dy[i].z * g.z * v[i].z + dy[i].w * g.w * v[i].w;
       }
+      const float m1 = warp_sum(s1) * (1.0f / H), m2 = warp_sum(s2) * (1.0f / H);
+      float4* r_dv = sbuf4 + (0 * kWarps + warp) * (H / 4);
+      float4* r_dx = sbuf4 + (1 * kWarps + warp) * (H / 4);
+      float4* r_dy = sbuf4 + (2 * kWarps + warp) * (H / 4);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        atomicAdd(&sacc[c + j], dv[j]);
-        atomicAdd(&sacc[H + c + j], dyv[j] * xh[j]);
-        atomicAdd(&sacc[2 * H + c + j], dyv[j]);
+      for (int i = 0; i < VPL; ++i) {
+        const int c4 = lane + 32 * i;
+        const float4 g = __ldg(g4 + c4);
+        const float4 dv = make_float4(rstd * (dy[i].x * g.x - m1 - v[i].x * m2), rstd * (dy[i].y * g.y - m1 - v[i].y * m2),
+                                      rstd * (dy[i].z * g.z - m1 - v[i].z * m2), rstd * (dy[i].w * g.w - m1 - v[i].w * m2));
+        if (s > 0) {
+          *reinterpret_cast<uint2*>(dconv + (static_cast<long long>(b) * (S - 1) + s - 1) * H + 4 * c4) =
+              make_uint2(pack_bf16x2(dv.x, dv.y), pack_bf16x2(dv.z, dv.w));
+        }
+        r_dv[c4] = dv;
+        r_dx[c4] = make_float4(dy[i].x * v[i].x, dy[i].y * v[i].y, dy[i].z * v[i].z, dy[i].w * v[i].w);
+        r_dy[c4] = dy[i];
       }
     }
+    __syncthreads();
+    const int nr = min(kWarps, B - b0);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = threadIdx.x + NT * j;
+      if (c < H) {
+        for (int r = 0; r < nr; ++r) {
+          apos[j] += sbuf[(0 * kWarps + r) * H + c];
+          ag[j] += sbuf[(1 * kWarps + r) * H + c];
+          ab[j] += sbuf[(2 * kWarps + r) * H + c];
+        }
+      }
+    }
+    __syncthreads();  // the buffers are rewritten by the next chunk
   }
-  __syncthreads();
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    dpos[static_cast<long long>(s) * H + c] += sacc[c];
-    if (s == 0) dcls[c] += sacc[c];
-    atomicAdd(dgamma + c, sacc[H + c]);
-    atomicAdd(dbeta + c, sacc[2 * H + c]);
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = threadIdx.x + NT * j;
+    if (c >= H) continue;
+    dpos[static_cast<long long>(s) * H + c] += apos[j];
+    if (s == 0) dcls[c] += apos[j];
+    atomicAdd(dgamma + c, ag[j]);
+    atomicAdd(dbeta + c, ab[j]);
   }
 }
 
@@ -664,7 +728,8 @@ void bert_embed_bwd(const torch::Tensor& ids, const torch::Tensor& tt, const tor
     d1 = dx1->data_ptr<float>();
   }
   c10::cuda::CUDAGuard guard(ids.device());
-  const int smem = (4 + T) * H * 4;
+  REVPP_CHECK(T <= kEmbedMaxTypes, "type vocabulary above ", kEmbedMaxTypes, " types");
+  const int smem = 3 * kWarps * H * 4;
   vpl_dispatch(H, [&](auto v) {
     auto k = bert_embed_bwd_kernel<decltype(v)::value>;
     if (smem > 48 * 1024) REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -725,9 +790,10 @@ void vit_assemble_bwd(const torch::Tensor& conv, const torch::Tensor& cls, const
   const int H = static_cast<int>(gamma.numel());
   c10::cuda::CUDAGuard guard(conv.device());
   const float* d1 = (dx1.has_value() && dx1->defined()) ? dx1->data_ptr<float>() : nullptr;
-  const int smem = 3 * H * 4;
+  const int smem = 3 * kWarps * H * 4;
   vpl_dispatch(H, [&](auto v) {
     auto k = vit_assemble_bwd_kernel<decltype(v)::value>;
+    if (smem > 48 * 1024) REVPP_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     k<<<static_cast<unsigned>(S), kWarps * 32, smem, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(conv.data_ptr()), cls.data_ptr<float>(), pos.data_ptr<float>(),
         gamma.data_ptr<float>(), static_cast<float>(eps), static_cast<int>(B), static_cast<int>(S),
