@@ -203,3 +203,23 @@ def test_launch_scripts_run_small(tmp_path, script):
     p = subprocess.run(["bash", os.path.join(ROOT, "launch", script)], capture_output=True, text=True, timeout=600,
                        cwd=ROOT, env=env)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+
+
+def test_bench_pipeline_defaults(monkeypatch):
+    """With a pipeline, this framework's arm uses copy-engine channels and interleaved 1F1B with
+    as many chunks per rank as the blocks allow (at most 3); NCCL groups and the reference arm
+    keep plain 1F1B."""
+    import importlib.util
+    import sys
+
+    spec = importlib.util.spec_from_file_location("bench_mod2", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cases = ((["--gpus", "1"], "1f1b", 1), (["--gpus", "2"], "interleaved", 3), (["--gpus", "8"], "interleaved", 3),
+             (["--gpus", "4", "--p2p", "group"], "1f1b", 1), (["--gpus", "8", "--impl", "reference"], "1f1b", 1))
+    for argv, sched, v in cases:
+        monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
+        a = bench.parse()
+        assert a.schedule == sched and a.virtual_stages == v, (argv, a.schedule, a.virtual_stages)
+        if "--p2p" not in argv:
+            assert a.p2p == "copy"
